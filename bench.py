@@ -1,0 +1,468 @@
+#!/usr/bin/env python
+"""Benchmark: sparse FP8 MLA decode step on B200 (BASELINE.json metric
+"sparse-decode us/step & % roofline").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1|2|4] [--mode batch|head]
+
+A step is one pass of the hot path over one batch: the decode kernel (K1)
+plus the split combine (K3), on the schedule that get_mla_metadata (K2)
+computed once for the batch (FlashMLA's protocol: metadata once per batch,
+reused by every layer; its own time is reported as sched_meta_us).
+Default workload: BASELINE config 1 (b 32, s_q 1, h_q 64, top-k 2048,
+128K-token context per request, page 256, random block tables, V32 FP8
+cache), synthetic seeded data.  L2 is flushed (256 MiB write) before every
+timed step; the gathered KV (43 MB) is below L2 size, so without the flush
+the rows would be L2-resident across steps.
+
+N > 1 (torchrun, one rank per GPU): "batch" mode shards requests -- every
+rank runs its own config-sized batch on its own cache (weak scaling, no
+collective in the data path); "head" mode splits h_q over the ranks with a
+replicated cache and all-gathers the bf16 outputs with NCCL (verification
+traffic, outside the timed step).  Timing: CUDA events on the launching
+stream, max over ranks.
+
+--impl reference times the CPU oracle port (oracle/, a numpy restatement
+of the reference's tests/reference.py) on this host's cores on the same
+workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "deepseek-v4-flash-sm120_b200"))
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 4])
+    ap.add_argument("--mode", choices=["batch", "head"], default="batch")
+    ap.add_argument("--batch", type=int, default=None, help="override b (per rank)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--json-out", default=None)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ peaks / clocks
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        self.gpu = ids[local_rank] if local_rank < len(ids) else str(local_rank)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", self.gpu, "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[3], f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"})
+        return {
+            "sm_mhz": statistics.median([r[0] for r in rows]) if rows else None,
+            "sm_max_mhz": max(r[1] for r in rows) if rows else None,
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+# ------------------------------------------------------------------ workload
+def workload(cfg: int, batch_override, rank: int):
+    from deepseek_v4_kernel import kvcache
+    spec = kvcache.CONFIGS[cfg]
+    spec = kvcache.BatchSpec(**{**spec.__dict__, "seed": 1000 + rank})
+    if batch_override:
+        spec.b = batch_override
+    return spec
+
+
+def algorithmic(spec, h_q_local=None):
+    h = h_q_local or spec.h_q
+    bpt = 656 if spec.layout == "v32" else 584
+    d_qk = 576 if spec.layout == "v32" else 512
+    rows = spec.b * spec.s_q * spec.topk
+    kv_bytes = rows * bpt
+    flops = 2.0 * spec.b * spec.s_q * h * spec.topk * (d_qk + 512)
+    return kv_bytes, flops
+
+
+def workload_name(spec, mode, world):
+    return (f"config{'' if spec is None else ''}: b{spec.b} s_q{spec.s_q} h_q{spec.h_q} "
+            f"topk{spec.topk} ctx{spec.ctx} page{spec.page_block} {spec.layout.upper()} fp8 KV"
+            + (f", {mode}-sharded x{world}" if world > 1 else ""))
+
+
+# ------------------------------------------------------------------ reference arm (CPU oracle)
+def run_reference(args, spec, world, rank):
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from threadpoolctl import threadpool_limits
+    from concurrent.futures import ThreadPoolExecutor
+
+    from deepseek_v4_kernel import kvcache
+    from oracle import sparse_decode_oracle as O
+
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    bt = kvcache.make_batch(spec, device=dev)
+    q = bt.q.float().cpu().numpy()
+    kv = bt.kv.cpu().numpy()
+    idx = bt.indices.cpu().numpy()
+    sink = bt.attn_sink.cpu().numpy() if bt.attn_sink is not None else None
+    del bt
+    threads = os.cpu_count() or 1
+
+    def one(rows):
+        return O.sparse_decode_reference(q[rows], kv, idx[rows], None, sink, 1.0 / math.sqrt(q.shape[-1]),
+                                         spec.page_block, layout=spec.layout)
+
+    # bounded sample: as many whole query rows as fit in ~2 s per step
+    t0 = time.perf_counter()
+    with threadpool_limits(1):
+        one([0])
+    per_row = max(time.perf_counter() - t0, 1e-4)
+    n_rows = int(min(spec.b, max(1, threads * 2.0 / per_row)))
+    chunks = [list(range(i, n_rows, threads)) for i in range(min(threads, n_rows))]
+    times = []
+    with threadpool_limits(1), ThreadPoolExecutor(threads) as ex:
+        for i in range(args.warmup + args.steps):
+            t = time.perf_counter()
+            list(ex.map(one, chunks))
+            dt = time.perf_counter() - t
+            if i >= args.warmup:
+                times.append(dt * spec.b / n_rows)       # scaled to the full batch
+    us = statistics.median(times) * 1e6
+    sample = (f"{n_rows} of {spec.b} query rows per step (times scaled to the full batch), "
+              f"numpy oracle port of tests/reference.py, gather of the top-k rows only")
+    line = {
+        "metric": "sparse_decode_us_per_step", "value": round(us, 1), "unit": "us/step",
+        "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(spec, args.mode, 1), "cpu_threads": threads},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_quick(spec, bt, budget_s=12.0):
+    """Oracle port timed on this host's cores on a bounded sample of the
+    workload (whole query rows), scaled to the full batch."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import sparse_decode_oracle as O
+
+    q = bt.q.float().cpu().numpy()
+    kv = bt.kv.cpu().numpy()
+    idx = bt.indices.cpu().numpy()
+    sink = bt.attn_sink.cpu().numpy() if bt.attn_sink is not None else None
+    threads = os.cpu_count() or 1
+
+    def one(rows):
+        return O.sparse_decode_reference(q[rows], kv, idx[rows], None, sink, bt.sm_scale,
+                                         spec.page_block, layout=spec.layout)
+
+    with threadpool_limits(1):
+        t0 = time.perf_counter()
+        one([0])
+        per_row = max(time.perf_counter() - t0, 1e-4)
+    n_rows = int(min(spec.b, max(threads, threads * (budget_s / 3) / per_row)))
+    n_rows = max(1, min(n_rows, spec.b))
+    chunks = [list(range(i, n_rows, threads)) for i in range(min(threads, n_rows))]
+    reps = []
+    with threadpool_limits(1), ThreadPoolExecutor(threads) as ex:
+        for _ in range(3):
+            t = time.perf_counter()
+            list(ex.map(one, chunks))
+            reps.append((time.perf_counter() - t) * spec.b / n_rows)
+    return {"value": round(statistics.median(reps) * 1e6, 1), "unit": "us/step", "cores": threads,
+            "kind": "port",
+            "sample": f"{n_rows} of {spec.b} query rows, 3 reps, median, scaled to the full batch; "
+                      f"numpy port of tests/reference.py (gathers only the top-k rows)"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, spec, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import deepseek_v4_kernel as dk
+    from deepseek_v4_kernel import _lib, kvcache, ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    lib = _lib.lib
+    assert lib.dsv4b_check_device(local_rank) == 0, "not an sm_100 GPU"
+
+    bt = kvcache.make_batch(spec, device=device)
+    h_lo, h_hi = 0, spec.h_q
+    if args.mode == "head" and world > 1:
+        from deepseek_v4_kernel import partition
+        h_lo, h_hi = partition.head_range(spec.h_q, rank, world)
+    q = bt.q[:, :, h_lo:h_hi].contiguous()
+    sink = bt.attn_sink[h_lo:h_hi].contiguous() if bt.attn_sink is not None else None
+    b, s_q, h_q, d_qk = q.shape
+    out = torch.empty(b, s_q, h_q, 512, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(b, h_q, s_q, dtype=torch.float32, device=device)
+    p = ops.build_params(q, bt.kv, bt.indices, None, sink, None, None, None, 512, bt.sm_scale, out, lse)
+    stream = torch.cuda.current_stream(device)
+    sh = stream.cuda_stream
+
+    # K2 once per batch (timed separately)
+    ev_s0, ev_s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev_s0.record()
+    tsm, ns = ops.get_mla_metadata_tensors(p, device)
+    ev_s1.record()
+    torch.cuda.synchronize()
+    sched_us = ev_s0.elapsed_time(ev_s1) * 1e3
+    parts = tsm.size(0)
+    nbytes = lib.dsv4b_workspace_bytes(b, s_q, h_q, parts)
+    ws = ops.workspace(device, nbytes)
+    pp = ctypes.byref(p)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def step(evs=None):
+        rc = lib.dsv4b_sparse_decode_partial(pp, tsm.data_ptr(), ns.data_ptr(), parts, ws.data_ptr(),
+                                             ws.numel(), sh)
+        if evs is not None:
+            evs[1].record(stream)
+        rc |= lib.dsv4b_combine(pp, ns.data_ptr(), parts, ws.data_ptr(), ws.numel(), sh)
+        if rc:
+            raise RuntimeError(f"decode failed: {rc}")
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.15)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        step(evs[i])
+        evs[i][2].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    dec_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    step_ms = [e[0].elapsed_time(e[2]) for e in evs]
+    t_step = statistics.median(step_ms)
+    t_dec = statistics.median(dec_ms)
+    assert dk.read_kernel_status(device) == 0, "kernel wait timeout"
+
+    # head mode: all-gather the head shards (verification traffic, untimed)
+    if args.mode == "head" and world > 1:
+        from deepseek_v4_kernel import partition
+        full = partition.all_gather_heads(out, world)
+        assert full.shape[2] == spec.h_q
+
+    # max over ranks
+    if world > 1:
+        t = torch.tensor([t_step, t_dec], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_step, t_dec = t.tolist()
+
+    # e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        q_host = q.cpu().pin_memory()
+        idx_host = bt.indices.cpu().pin_memory()
+        q_dev = torch.empty_like(q)
+        idx_dev = torch.empty_like(bt.indices)
+        out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        lse_host = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+        meta, _ = dk.get_mla_metadata()
+        n_e2e = max(1, min(args.steps, 200))
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            idx_dev.copy_(idx_host, non_blocking=True)
+            o, l = dk.flash_mla_with_kvcache(q_dev, bt.kv, None, None, 512, meta, softmax_scale=bt.sm_scale,
+                                             is_fp8_kvcache=True, indices=idx_dev, attn_sink=sink)
+            out_host.copy_(o, non_blocking=True)
+            lse_host.copy_(l, non_blocking=True)
+
+        for _ in range(3):
+            flush.zero_()
+            e2e_step()
+        torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_e2e)]
+        for i in range(n_e2e):
+            flush.zero_()
+            ev[i][0].record(stream)
+            e2e_step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        t_e2e = statistics.median([a.elapsed_time(b_) for a, b_ in ev])
+        if world > 1:
+            t = torch.tensor([t_e2e], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = t.item()
+        h2d = q_host.numel() * q_host.element_size() + idx_host.numel() * idx_host.element_size()
+        d2h = out_host.numel() * out_host.element_size() + lse_host.numel() * lse_host.element_size()
+        e2e = {"value": round(t_e2e * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h,
+               "path": "deepseek_v4_kernel.flash_mla_with_kvcache (FlashMLASchedMeta reused), "
+                       "pinned host q/indices -> device, out/lse -> pinned host"}
+
+    if rank != 0:
+        return
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    kv_bytes, flops = algorithmic(spec, h_q)
+    achieved_gbs = kv_bytes / (t_dec * 1e-3) / 1e9
+    achieved_tf = flops / (t_dec * 1e-3) / 1e12
+    bound = "hbm" if kv_bytes / hbm_peak / 1e9 >= flops / tc_peak / 1e12 else "tensor"
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get(f"config{args.config}")
+        except Exception:
+            traffic = None
+    if bound == "hbm":
+        roof = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic}
+    else:
+        roof = {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                "frac": round(achieved_tf / tc_peak, 4), "traffic": traffic}
+    roof["peak_source"] = peak_src
+    roof["kernel"] = "sparse_decode_kernel (K1)"
+    roof["algorithmic_bytes_per_launch"] = kv_bytes
+    roof["algorithmic_flops_per_launch"] = flops
+    roof["tensor_frac"] = round(achieved_tf / tc_peak, 4)
+    roof["hbm_frac"] = round(achieved_gbs / hbm_peak, 4)
+    t_roof_us = max(kv_bytes / hbm_peak / 1e3, flops / tc_peak / 1e6)
+    tokens = spec.b * spec.s_q * world if args.mode == "batch" else spec.b * spec.s_q
+    line = {
+        "metric": "sparse_decode_us_per_step",
+        "value": round(t_step * 1e3, 2),
+        "unit": "us/step",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step, 5),
+        "higher_is_better": False,
+        "scaling": "weak" if args.mode == "batch" else "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q / latent / RoPE, random page tables, distinct top-k)",
+        "config": {"workload": f"config{args.config} " + workload_name(spec, args.mode, world),
+                   "l2": "flushed before every step (256 MiB write)",
+                   "parallelism": f"{args.mode}-shard x{world}" if world > 1 else "single GPU",
+                   "num_sm_parts": parts},
+        "decode_kernel_us": round(t_dec * 1e3, 2),
+        "combine_us": round((t_step - t_dec) * 1e3, 2),
+        "sched_meta_us": round(sched_us, 2),
+        "roofline_time_us": round(t_roof_us, 2),
+        "step_roofline_frac": round(t_roof_us / (t_step * 1e3), 4),
+        "tokens_per_s": round(tokens / (t_step * 1e-3), 1),
+        "roofline": roof,
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_quick(spec, bt)
+    print(json.dumps(line), flush=True)
+    if args.json_out:
+        with open(args.json_out, "w") as f:
+            f.write(json.dumps(line) + "\n")
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    spec = workload(args.config, args.batch, rank if args.mode == "batch" else 0)
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, spec, world, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, spec, world, rank, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,229 @@
+// C ABI entry points (include/dsv4b.h): argument validation, workspace
+// carving, and the launch sequence.  Replaces the ATen host wrapper of the
+// reference (csrc/api/sparse_decode.cpp:29-172): same checks, but status
+// codes instead of TORCH_CHECK / abort(), no per-call
+// cudaGetDeviceProperties, no output transpose copy.
+#include <climits>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+
+#include "dsv4b.h"
+#include "dsv4b_kernels.h"
+
+namespace {
+
+constexpr size_t kStatusBytes = 256;
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t lse_off, o_off, total;
+};
+
+inline WsLayout ws_layout(int b, int s_q, int h_q, int parts) {
+  const size_t max_splits = (size_t)b * s_q + (size_t)parts;
+  WsLayout w;
+  w.lse_off = kStatusBytes;
+  w.o_off = align_up(w.lse_off + max_splits * h_q * sizeof(float), 256);
+  w.total = align_up(w.o_off + max_splits * h_q * 512 * sizeof(float), 256);
+  return w;
+}
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_cache(int layout, const void* kv, int num_blocks, int page, int64_t stride_block,
+                int64_t stride_row) {
+  if (!kv || num_blocks <= 0 || page <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((int64_t)num_blocks * page > INT_MAX) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(kv, 16) || stride_block % 16 != 0) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (layout == DSV4B_LAYOUT_V32) {
+    if (stride_row < 656 || stride_row % 16 != 0) return DSV4B_ERR_INVALID_ARGUMENT;
+    if (stride_block < (int64_t)(page - 1) * stride_row + 656) return DSV4B_ERR_INVALID_ARGUMENT;
+  } else {
+    if (stride_block < (int64_t)page * 584) return DSV4B_ERR_INVALID_ARGUMENT;
+  }
+  return DSV4B_OK;
+}
+
+int check_params(const dsv4b_decode_params* p) {
+  if (!p) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->layout != DSV4B_LAYOUT_V32 && p->layout != DSV4B_LAYOUT_MODEL1) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->b <= 0 || p->s_q <= 0 || p->h_q <= 0 || p->topk <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((int64_t)p->b * p->s_q > dsv4b::kMaxSchedRows) return DSV4B_ERR_UNSUPPORTED;
+  if (p->d_v != 512) return DSV4B_ERR_UNSUPPORTED;
+  if (p->d_qk != (p->layout == DSV4B_LAYOUT_V32 ? 576 : 512)) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!p->q || !p->indices || !p->out || !p->lse) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->q, 16) || p->stride_q_b % 8 || p->stride_q_s % 8 || p->stride_q_h % 8)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->out, 8) || p->stride_o_b % 4 || p->stride_o_s % 4 || p->stride_o_h % 4)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->lse, 4) || !aligned(p->indices, 4)) return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = check_cache(p->layout, p->kv, p->num_blocks, p->page_block_size, p->stride_kv_block,
+                       p->stride_kv_row);
+  if (rc) return rc;
+  if (p->extra_kv) {
+    if (!p->extra_indices || p->extra_topk < 0) return DSV4B_ERR_INVALID_ARGUMENT;
+    rc = check_cache(p->layout, p->extra_kv, p->extra_num_blocks, p->extra_page_block_size,
+                     p->stride_extra_kv_block, p->stride_extra_kv_row);
+    if (rc) return rc;
+  }
+  return DSV4B_OK;
+}
+
+struct DevInfo {
+  bool init = false;
+  int major = 0, minor = 0, sms = 0;
+};
+DevInfo g_dev[64];
+
+int dev_info(int device, DevInfo** out) {
+  if (device < 0 || device >= 64) return DSV4B_ERR_INVALID_ARGUMENT;
+  DevInfo& d = g_dev[device];
+  if (!d.init) {
+    if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+      return DSV4B_ERR_CUDA;
+    d.init = true;
+  }
+  *out = &d;
+  return DSV4B_OK;
+}
+
+int current_arch_ok() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSV4B_ERR_CUDA;
+  return dsv4b_check_device(dev);
+}
+
+int cuda_rc(cudaError_t e) {
+  if (e == cudaSuccess) return DSV4B_OK;
+  if (getenv("DSV4B_VERBOSE")) fprintf(stderr, "dsv4b: CUDA error %s\n", cudaGetErrorString(e));
+  return DSV4B_ERR_CUDA;
+}
+
+int check_workspace(const dsv4b_decode_params* p, int parts, void* ws, size_t ws_bytes,
+                    WsLayout* w) {
+  if (parts <= 0 || parts > 65535) return DSV4B_ERR_INVALID_ARGUMENT;
+  *w = ws_layout(p->b, p->s_q, p->h_q, parts);
+  if (!ws || !aligned(ws, 256) || ws_bytes < w->total) return DSV4B_ERR_WORKSPACE;
+  return DSV4B_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dsv4b_version(void) { return 100; }
+
+const char* dsv4b_status_string(int status) {
+  switch (status) {
+    case DSV4B_OK: return "ok";
+    case DSV4B_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case DSV4B_ERR_UNSUPPORTED: return "unsupported configuration";
+    case DSV4B_ERR_CUDA: return "CUDA runtime error";
+    case DSV4B_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case DSV4B_ERR_ARCH: return "device is not an sm_100 (B200-class) GPU";
+    case DSV4B_ERR_KERNEL_TIMEOUT: return "a kernel wait hit its time limit";
+    default: return "unknown status";
+  }
+}
+
+int dsv4b_check_device(int device) {
+  DevInfo* d = nullptr;
+  const int rc = dev_info(device, &d);
+  if (rc) return rc;
+  return (d->major == 10 && d->minor == 0) ? DSV4B_OK : DSV4B_ERR_ARCH;
+}
+
+int dsv4b_num_sm_parts(int device, int h_q, int32_t* num_sm_parts) {
+  if (!num_sm_parts || h_q <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
+  DevInfo* d = nullptr;
+  const int rc = dev_info(device, &d);
+  if (rc) return rc;
+  const int groups = (h_q + dsv4b::kHeadsPerCtaPublic - 1) / dsv4b::kHeadsPerCtaPublic;
+  const int parts = d->sms / groups;
+  *num_sm_parts = parts > 0 ? parts : 1;
+  return DSV4B_OK;
+}
+
+size_t dsv4b_workspace_bytes(int b, int s_q, int h_q, int num_sm_parts) {
+  if (b <= 0 || s_q <= 0 || h_q <= 0 || num_sm_parts <= 0) return 0;
+  return ws_layout(b, s_q, h_q, num_sm_parts).total;
+}
+
+int dsv4b_get_mla_metadata(const dsv4b_decode_params* p, int num_sm_parts,
+                           dsv4b_sched_meta* sched_meta, int32_t* num_splits, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (num_sm_parts <= 0 || num_sm_parts > 65535 || !sched_meta || !num_splits)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((rc = current_arch_ok())) return rc;
+  return cuda_rc(dsv4b::launch_sched_meta(*p, num_sm_parts, sched_meta, num_splits,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_sparse_decode_partial(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
+                                const int32_t* num_splits, int num_sm_parts, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (!sched_meta || !num_splits) return DSV4B_ERR_INVALID_ARGUMENT;
+  WsLayout w;
+  if ((rc = check_workspace(p, num_sm_parts, workspace, workspace_bytes, &w))) return rc;
+  if ((rc = current_arch_ok())) return rc;
+  char* ws = static_cast<char*>(workspace);
+  return cuda_rc(dsv4b::launch_sparse_decode(
+      *p, sched_meta, num_splits, num_sm_parts, reinterpret_cast<float*>(ws + w.lse_off),
+      reinterpret_cast<float*>(ws + w.o_off), reinterpret_cast<int*>(ws),
+      static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_combine(const dsv4b_decode_params* p, const int32_t* num_splits, int num_sm_parts,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (!num_splits) return DSV4B_ERR_INVALID_ARGUMENT;
+  WsLayout w;
+  if ((rc = check_workspace(p, num_sm_parts, workspace, workspace_bytes, &w))) return rc;
+  char* ws = static_cast<char*>(workspace);
+  return cuda_rc(dsv4b::launch_combine(*p, num_splits, reinterpret_cast<const float*>(ws + w.lse_off),
+                                       reinterpret_cast<const float*>(ws + w.o_off),
+                                       static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_sparse_decode(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
+                        const int32_t* num_splits, int num_sm_parts, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  const int rc = dsv4b_sparse_decode_partial(p, sched_meta, num_splits, num_sm_parts, workspace,
+                                             workspace_bytes, stream);
+  if (rc) return rc;
+  return dsv4b_combine(p, num_splits, num_sm_parts, workspace, workspace_bytes, stream);
+}
+
+int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks, int page_block_size,
+                         int64_t stride_kv_block, int64_t stride_kv_row, const int32_t* indices,
+                         int n, void* out_bf16, void* stream) {
+  if (layout != DSV4B_LAYOUT_V32 && layout != DSV4B_LAYOUT_MODEL1) return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = check_cache(layout, kv, num_blocks, page_block_size, stride_kv_block, stride_kv_row);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (!indices || !out_bf16 || !aligned(out_bf16, 16))))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (n == 0) return DSV4B_OK;
+  if ((rc = current_arch_ok())) return rc;
+  return cuda_rc(dsv4b::launch_gather_dequant(layout, kv, num_blocks, page_block_size, stride_kv_block,
+                                              stride_kv_row, indices, n, out_bf16,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes, int* flags, void* stream) {
+  if (!workspace || workspace_bytes < kStatusBytes || !flags) return DSV4B_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = cuda_rc(cudaMemcpyAsync(flags, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (rc) return rc;
+  if ((rc = cuda_rc(cudaStreamSynchronize(s)))) return rc;
+  return cuda_rc(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+}
+
+}  // extern "C"

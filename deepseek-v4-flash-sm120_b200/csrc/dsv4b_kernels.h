@@ -1,0 +1,35 @@
+// Host-side launch functions of the device kernels (internal to the
+// library; the public surface is include/dsv4b.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "dsv4b.h"
+
+namespace dsv4b {
+
+// Largest b * s_q the on-device scheduler accepts (its per-row tables
+// live in shared memory).
+constexpr int kMaxSchedRows = 16384;
+
+// Query heads handled by one decode CTA (UMMA N).
+constexpr int kHeadsPerCtaPublic = 64;
+
+cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                                 const int32_t* num_splits, int num_sm_parts, float* lse_accum,
+                                 float* o_accum, int* err, cudaStream_t stream);
+
+int decode_smem_bytes(int layout);
+
+cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
+                              dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream);
+
+cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
+                           const float* lse_accum, const float* o_accum, cudaStream_t stream);
+
+cudaError_t launch_gather_dequant(int layout, const void* kv, int num_blocks, int page_block_size,
+                                  int64_t stride_kv_block, int64_t stride_kv_row,
+                                  const int32_t* indices, int n, void* out_bf16,
+                                  cudaStream_t stream);
+
+}  // namespace dsv4b

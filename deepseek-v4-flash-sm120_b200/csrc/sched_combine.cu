@@ -1,0 +1,278 @@
+// K2 get_mla_metadata (split-KV tile scheduler), K3 split combine, and the
+// debug row gather.
+//
+// K2 replaces the reference's placeholder scheduler tensors
+// (csrc/api/sparse_decode.cpp:147-158, num_sm_parts = 1) with a real
+// plan: every query row r = b*s_q + s owns ceil(len/128) main tiles plus
+// ceil(extra_len/128) extra tiles; the concatenated tile list is cut into
+// min(num_sm_parts, total tiles) contiguous, equal (+-1 tile) ranges, one
+// per decode CTA column.  A row cut by a range boundary becomes several
+// splits whose partial (O, LSE) the combine kernel merges.  Everything
+// runs on the device (one CTA), so a captured CUDA graph replays it.
+//
+// K3 merges splits: lse = log sum_i exp(lse_i), O = sum_i exp(lse_i - lse)
+// O_i, then the sink epilogue of tests/reference.py:124-129.  One warp per
+// (query row, head); rows with a single split were written by K1 directly.
+#include <cuda_bf16.h>
+
+#include "dsv4b_internal.cuh"
+#include "dsv4b_kernels.h"
+
+namespace dsv4b {
+
+namespace {
+
+constexpr int kSchedThreads = 1024;
+
+// Exclusive block-wide scan of v over kSchedThreads threads; returns the
+// prefix for this thread and writes the block total to *total.
+__device__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = scratch[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    scratch[lane] = w;  // inclusive per-warp totals
+  }
+  __syncthreads();
+  const int warp_prefix = warp > 0 ? scratch[warp - 1] : 0;
+  *total = scratch[31];
+  __syncthreads();
+  return warp_prefix + x - v;
+}
+
+// Part that owns global tile t when T tiles are split into P ranges
+// [floor(pT/P), floor((p+1)T/P)): the largest p with floor(pT/P) <= t.
+__device__ __forceinline__ int part_of_tile(long long t, long long T, long long P) {
+  return (int)(((t + 1) * P + T - 1) / T) - 1;
+}
+
+__global__ void __launch_bounds__(kSchedThreads)
+    sched_meta_kernel(const dsv4b_decode_params p, int num_sm_parts, dsv4b_sched_meta* sched,
+                      int32_t* num_splits) {
+  extern __shared__ int sh[];
+  const int R = p.b * p.s_q;
+  int* tile_off = sh;          // [R + 1]
+  int* scratch = sh + R + 1;   // [32]
+
+  // 1. tiles per query row -> exclusive prefix
+  int carry = 0;
+  for (int base = 0; base < R; base += kSchedThreads) {
+    const int r = base + threadIdx.x;
+    const int n = r < R ? req_info(p, r).nt : 0;
+    int tot;
+    const int ex = block_exclusive_scan(n, scratch, &tot);
+    if (r < R) tile_off[r] = carry + ex;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) tile_off[R] = carry;
+  __syncthreads();
+  const long long T = tile_off[R];
+  const int P_eff = (int)min((long long)num_sm_parts, T);
+
+  // 2. splits per row -> exclusive prefix = num_splits
+  carry = 0;
+  for (int base = 0; base < R; base += kSchedThreads) {
+    const int r = base + threadIdx.x;
+    int n = 0;
+    if (r < R) {
+      const int first = part_of_tile(tile_off[r], T, P_eff);
+      const int last = part_of_tile(tile_off[r + 1] - 1, T, P_eff);
+      n = last - first + 1;
+    }
+    int tot;
+    const int ex = block_exclusive_scan(n, scratch, &tot);
+    if (r < R) num_splits[r] = carry + ex;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) {
+    num_splits[R] = carry;
+  }
+  __syncthreads();
+
+  // 3. one record per part
+  for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+    dsv4b_sched_meta m;
+    if (part >= P_eff) {
+      m.begin_req_idx = 0;
+      m.end_req_idx = -1;
+      m.begin_block_idx = m.end_block_idx = 0;
+      m.begin_split_idx = 0;
+      m.is_first_req_splitted = m.is_last_req_splitted = 0;
+      m.num_tiles = 0;
+    } else {
+      const long long t0 = (long long)part * T / P_eff;
+      const long long t1 = (long long)(part + 1) * T / P_eff;  // exclusive, > t0
+      // row containing tile x: largest r with tile_off[r] <= x
+      auto row_of = [&](long long x) {
+        int lo = 0, hi = R - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (tile_off[mid] <= x) lo = mid; else hi = mid - 1;
+        }
+        return lo;
+      };
+      const int br = row_of(t0), er = row_of(t1 - 1);
+      m.begin_req_idx = br;
+      m.end_req_idx = er;
+      m.begin_block_idx = (int)(t0 - tile_off[br]);
+      m.end_block_idx = (int)(t1 - tile_off[er]);
+      m.begin_split_idx = num_splits[br] + (part - part_of_tile(tile_off[br], T, P_eff));
+      m.is_first_req_splitted = m.begin_block_idx > 0;
+      m.is_last_req_splitted = (tile_off[er] + m.end_block_idx) < tile_off[er + 1];
+      m.num_tiles = (int)(t1 - t0);
+    }
+    sched[part] = m;
+  }
+}
+
+// ------------------------------------------------------------- combine
+constexpr int kCombineWarps = 8;
+
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    combine_kernel(const dsv4b_decode_params p, const int32_t* __restrict__ num_splits,
+                   const float* __restrict__ lse_accum, const float* __restrict__ o_accum) {
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y * kCombineWarps + warp;
+  if (head >= p.h_q) return;
+  const int s0 = __ldg(num_splits + r), s1 = __ldg(num_splits + r + 1);
+  const int n = s1 - s0;
+  if (n <= 1) return;  // written by the decode kernel
+
+  float mx = -INFINITY;
+  for (int i = lane; i < n; i += 32) mx = fmaxf(mx, __ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.0f;
+  for (int i = lane; i < n; i += 32) sum += expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  float lse = mx + logf(sum);
+
+  float4 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < n; ++i) {
+    const float w = expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - lse);
+    const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)(s0 + i) * p.h_q + head) * kDv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 v = __ldg(src + lane + 32 * k);
+      acc[k].x = fmaf(w, v.x, acc[k].x);
+      acc[k].y = fmaf(w, v.y, acc[k].y);
+      acc[k].z = fmaf(w, v.z, acc[k].z);
+      acc[k].w = fmaf(w, v.w, acc[k].w);
+    }
+  }
+  float scale = 1.0f;
+  if (p.attn_sink) {
+    const float sink = __ldg(p.attn_sink + head);
+    scale = 1.0f / (1.0f + expf(sink - lse));
+    if (p.lse_includes_sink) {
+      const float m = fmaxf(lse, sink);
+      lse = m + logf(expf(lse - m) + expf(sink - m));
+    }
+  }
+  const int b = r / p.s_q, s = r - b * p.s_q;
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.stride_o_b +
+                       (int64_t)s * p.stride_o_s + (int64_t)head * p.stride_o_h;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[k].x * scale, acc[k].y * scale);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc[k].z * scale, acc[k].w * scale);
+    uint2 v;
+    v.x = *reinterpret_cast<const uint32_t*>(&lo);
+    v.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(out + 4 * (lane + 32 * k)) = v;
+  }
+  if (lane == 0) p.lse[((int64_t)b * p.h_q + head) * p.s_q + s] = lse;
+}
+
+// ------------------------------------------------------------- debug gather
+// One thread per (row, half): the exact producer path of K1 (same loads,
+// same dq16), written to a plain row-major [n, d_qk] bf16 array.
+template <int L>
+__global__ void gather_dequant_kernel(const uint8_t* kv, int num_blocks, int page,
+                                      int64_t stride_block, int64_t stride_row,
+                                      const int32_t* __restrict__ idx, int n,
+                                      __nv_bfloat16* __restrict__ out) {
+  using LT = LayoutT<L>;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = t >> 1, half = t & 1;
+  if (row >= n) return;
+  const RowSrc r = row_src<L>(kv, page, stride_block, stride_row, num_blocks * page, __ldg(idx + row), true);
+  const uint4 sc = load_scales<L>(r);
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * LT::kDqk);
+  for (int c = 0; c < LT::kFp8Chunks; ++c) {
+    uint4 a, b, o0, o1, o2, o3;
+    load_fp8_half<L>(r, c, half, a, b);
+    const float s = chunk_scale<L>(sc, c);
+    dq16(a, s, o0, o1);
+    dq16(b, s, o2, o3);
+    uint4* d = dst + c * 8 + half * 4;
+    d[0] = o0; d[1] = o1; d[2] = o2; d[3] = o3;
+  }
+  uint4 rope[4];
+  load_rope_half<L>(r, half, rope);
+  uint4* d = dst + LT::kFp8Chunks * 8 + half * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = rope[i];
+}
+
+}  // namespace
+
+cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
+                              dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream) {
+  const int R = p.b * p.s_q;
+  const size_t smem = (size_t)(R + 1 + 32) * sizeof(int);
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    e = cudaFuncSetAttribute(sched_meta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((kMaxSchedRows + 1 + 32) * sizeof(int)));
+    if (e != cudaSuccess) return e;
+    attr_done[dev] = true;
+  }
+  sched_meta_kernel<<<1, kSchedThreads, smem, stream>>>(p, num_sm_parts, sched, num_splits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
+                           const float* lse_accum, const float* o_accum, cudaStream_t stream) {
+  const dim3 grid(p.b * p.s_q, (p.h_q + kCombineWarps - 1) / kCombineWarps);
+  combine_kernel<<<grid, kCombineWarps * 32, 0, stream>>>(p, num_splits, lse_accum, o_accum);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_dequant(int layout, const void* kv, int num_blocks, int page_block_size,
+                                  int64_t stride_kv_block, int64_t stride_kv_row,
+                                  const int32_t* indices, int n, void* out_bf16,
+                                  cudaStream_t stream) {
+  const int threads = 256;
+  const int blocks = (2 * n + threads - 1) / threads;
+  if (layout == DSV4B_LAYOUT_V32)
+    gather_dequant_kernel<DSV4B_LAYOUT_V32><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint8_t*>(kv), num_blocks, page_block_size, stride_kv_block, stride_kv_row,
+        indices, n, static_cast<__nv_bfloat16*>(out_bf16));
+  else
+    gather_dequant_kernel<DSV4B_LAYOUT_MODEL1><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint8_t*>(kv), num_blocks, page_block_size, stride_kv_block, stride_kv_row,
+        indices, n, static_cast<__nv_bfloat16*>(out_bf16));
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4b

@@ -1,0 +1,590 @@
+// K1: sparse FP8 MLA decode for sm_100a (tcgen05 / TMEM).
+//
+// Replaces the reference's CUDA-core kernel
+// (csrc/sm120/decode/sparse_decode_kernel.cuh:202-403).  Same math
+// (tests/reference.py:105-131): gather top-k rows by flat index, dequantise
+// FP8 to bf16, S = Q K^T * scale, softmax over the positions, O = P V,
+// sink epilogue.  Different machine mapping:
+//
+//  * One CTA = one scheduler part (a run of 128-position tiles of one or
+//    more query rows, from get_mla_metadata) x one group of 64 heads.
+//  * S is computed transposed, S^T[tok, head] = K_tile . Q^T, so the 128
+//    tokens of a tile are the UMMA M dimension (M = 128, full tensor rate)
+//    and the 64 heads are N.  O is computed transposed as well,
+//    O^T[dim, head] += V^T . P^T, with V^T read MN-major straight out of
+//    the same bf16 K tile (4 M-blocks of 128 dims).
+//  * TMEM (512 columns): S^T [0,64), O^T [64,320), per-thread partial
+//    softmax row sums [320,384).
+//  * Shared memory: Q^T (64 heads x d_qk bf16, 72 KB for V32) and a ring of
+//    d_qk/64 chunk slots, each a 128-token x 64-column bf16 SWIZZLE_128B
+//    tile (16 KB).  PV M-block m releases slots 2m, 2m+1, so the next
+//    tile's dequant overlaps the current PV.  V32 writes P^T into the RoPE
+//    slot (RoPE is not part of V); MODEL1 has a separate P^T buffer.
+//
+// Warp roles (416 threads):
+//   warps 0-7   producers: per tile, each thread owns one token row and
+//               one 32-column half of every chunk; loads raw FP8 / scales /
+//               RoPE with 16-byte loads one tile ahead, dequantises, stores
+//               swizzled bf16; also loads Q^T at each query-row change and
+//               issues L2 bulk prefetches two tiles ahead.
+//   warps 8-11  softmax + epilogue: thread = token row = TMEM lane;
+//               column max via redux.sync + a 4-warp exchange, lazy
+//               rescaling (only when a head's max grows by > 2^8), P^T to
+//               shared memory, row sums in TMEM, final normalisation, sink,
+//               LSE and the output / split-partial store.
+//   warp 12     TMEM allocation and the single-thread tcgen05.mma issuer.
+//
+// All mbarrier waits are bounded (dsv4b_ptx.cuh: mbar_wait); on a timeout
+// the CTA raises an abort flag, every role leaves its loop, TMEM is freed
+// and the workspace status word records kErrWaitTimeout.
+#include <cuda_bf16.h>
+
+#include "dsv4b_internal.cuh"
+#include "dsv4b_kernels.h"
+
+namespace dsv4b {
+
+namespace {
+
+constexpr int kProducerWarps = 8;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kThreads = (kProducerWarps + kSoftmaxWarps + 1) * 32;  // 416
+constexpr int kProducerThreads = kProducerWarps * 32;
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kMmaWarp = kProducerWarps + kSoftmaxWarps;
+
+constexpr int kQChunkBytes = kHeadsPerCta * 128;       // 8 KB
+constexpr int kSlotBytes = kTileTokens * 128;          // 16 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 64, kColL = 320;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct Misc {
+  uint64_t full[9];
+  uint64_t empty[5];
+  uint64_t s_full, p_full, q_full, q_empty, o_full;
+  uint32_t tmem_base;
+  int abort;
+  int pad[2];
+  float red[4][64];
+  float m_use[64];
+  float alpha[64];
+  float scale_o[64];
+};
+
+template <int L>
+struct SmemPlan {
+  static constexpr int kChunks = LayoutT<L>::kChunks;
+  static constexpr int kQOff = 0;
+  static constexpr int kSlotOff = kChunks * kQChunkBytes;
+  static constexpr int kPOff = LayoutT<L>::kPInRopeSlot ? kSlotOff + (kChunks - 1) * kSlotBytes
+                                                        : kSlotOff + kChunks * kSlotBytes;
+  static constexpr int kMiscOff =
+      kSlotOff + kChunks * kSlotBytes + (LayoutT<L>::kPInRopeSlot ? 0 : kSlotBytes);
+  static constexpr int kBytes = kMiscOff + (int)sizeof(Misc) + 1024;  // + alignment slack
+};
+
+static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kBytes <= 232448, "V32 smem plan too large");
+static_assert(SmemPlan<DSV4B_LAYOUT_MODEL1>::kBytes <= 232448, "MODEL1 smem plan too large");
+
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 o = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&o);
+}
+
+// Empty barrier guarding chunk slot c.
+template <int L>
+__device__ __forceinline__ int empty_of(int c) {
+  return (LayoutT<L>::kPInRopeSlot && c == LayoutT<L>::kChunks - 1) ? 4 : (c >> 1);
+}
+
+// ------------------------------------------------------------- producers
+template <int L>
+struct ProducerRegs {
+  // FP8 chunks 0-3 (A half of the tile), their scales, then the rest.
+  uint4 a[8];
+  uint4 sc;
+  uint4 b[2 * (LayoutT<L>::kFp8Chunks - 4) + 4];
+};
+
+template <int L>
+__device__ __forceinline__ RowSrc producer_row(const dsv4b_decode_params& p, const TileCursor& c,
+                                               int row) {
+  const TileSpan ts = tile_span(p, c);
+  const bool in_range = row < ts.npos;
+  const int idx = in_range ? __ldg(ts.idx + row) : -1;
+  return row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx, in_range);
+}
+
+template <int L>
+__device__ __forceinline__ void prefetch_row_l2(const RowSrc& r) {
+  if (!r.valid) return;
+  if constexpr (L == DSV4B_LAYOUT_V32) {
+    prefetch_l2_bulk(r.rec, LayoutT<L>::kRecordBytes);
+  } else {
+    prefetch_l2_bulk(r.rec, LayoutT<L>::kRowBytes);
+    prefetch_l2_bulk(reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(r.scl) & ~uintptr_t(15)),
+                     16);
+  }
+}
+
+template <int L>
+__device__ __forceinline__ void load_part_a(const RowSrc& r, int half, ProducerRegs<L>& R) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) load_fp8_half<L>(r, c, half, R.a[2 * c], R.a[2 * c + 1]);
+  R.sc = load_scales<L>(r);
+}
+
+template <int L>
+__device__ __forceinline__ void load_part_b(const RowSrc& r, int half, ProducerRegs<L>& R) {
+  constexpr int nf = LayoutT<L>::kFp8Chunks;
+#pragma unroll
+  for (int c = 4; c < nf; ++c) load_fp8_half<L>(r, c, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1]);
+  uint4 rope[4];
+  load_rope_half<L>(r, half, rope);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) R.b[2 * (nf - 4) + i] = rope[i];
+}
+
+__device__ __forceinline__ void store_fp8_chunk(uint32_t slot, int row, int half, uint4 a, uint4 b,
+                                                float s) {
+  uint4 o0, o1, o2, o3;
+  dq16(a, s, o0, o1);
+  dq16(b, s, o2, o3);
+  sts_v4(slot + sw128_off(row, 4 * half + 0), o0);
+  sts_v4(slot + sw128_off(row, 4 * half + 1), o1);
+  sts_v4(slot + sw128_off(row, 4 * half + 2), o2);
+  sts_v4(slot + sw128_off(row, 4 * half + 3), o3);
+}
+
+template <int L>
+__device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
+                             uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
+  using LT = LayoutT<L>;
+  constexpr int NCH = LT::kChunks;
+  constexpr int NF = LT::kFp8Chunks;
+  const int ptid = threadIdx.x;
+  const int row = ptid >> 1, half = ptid & 1;
+
+  TileCursor cur = cursor_begin(p, sm);
+  if (!cur.valid) return;
+  TileCursor nxt = cursor_next(p, sm, cur);
+
+  ProducerRegs<L> R;
+  RowSrc rs = producer_row<L>(p, cur, row);
+  if (half == 0) prefetch_row_l2<L>(rs);
+  load_part_a<L>(rs, half, R);
+  load_part_b<L>(rs, half, R);
+
+  int tile_count = 0, seg_count = 0;
+  volatile int* abort_flag = &M.abort;
+  while (cur.valid) {
+    if (cur.t == cur.t_lo) {
+      // New query row: (re)load Q^T once the previous row's last QK^T is done.
+      if (seg_count > 0 && !mbar_wait(&M.q_empty, (seg_count - 1) & 1, abort_flag, err)) return;
+      const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
+                                (int64_t)cur.ri.b * p.stride_q_b + (int64_t)cur.ri.s * p.stride_q_s;
+      for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
+        const int j = i / (NCH * 8);
+        const int rem = i - j * (NCH * 8);
+        const int c = rem >> 3, u = rem & 7;
+        const int head = g * kHeadsPerCta + j;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (head < p.h_q) v = ldg_nc_v4(qb + (int64_t)head * p.stride_q_h + c * 64 + u * 8);
+        sts_v4(q_s + c * kQChunkBytes + sw128_off(j, u), v);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&M.q_full);
+      ++seg_count;
+    }
+
+    RowSrc rs_next;
+    rs_next.valid = false;
+    if (nxt.valid) {
+      rs_next = producer_row<L>(p, nxt, row);
+      if (half == 0) prefetch_row_l2<L>(rs_next);
+    }
+
+    const uint4 sc = R.sc;
+    const uint32_t wait_par = (tile_count - 1) & 1;
+
+    // FP8 chunks 0..3 from R.a
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (tile_count > 0 && !mbar_wait(&M.empty[empty_of<L>(c)], wait_par, abort_flag, err)) return;
+      store_fp8_chunk(slot_s + c * kSlotBytes, row, half, R.a[2 * c], R.a[2 * c + 1],
+                      chunk_scale<L>(sc, c));
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[c]);
+    }
+    if (nxt.valid) load_part_a<L>(rs_next, half, R);
+
+    // FP8 chunks 4..NF-1 and the RoPE chunk from R.b
+#pragma unroll
+    for (int c = 4; c < NCH; ++c) {
+      if (tile_count > 0 && !mbar_wait(&M.empty[empty_of<L>(c)], wait_par, abort_flag, err)) return;
+      const uint32_t slot = slot_s + c * kSlotBytes;
+      if (c < NF) {
+        store_fp8_chunk(slot, row, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1],
+                        chunk_scale<L>(sc, c));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sts_v4(slot + sw128_off(row, 4 * half + i), R.b[2 * (NF - 4) + i]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[c]);
+    }
+    if (nxt.valid) load_part_b<L>(rs_next, half, R);
+
+    cur = nxt;
+    nxt = cursor_next(p, sm, nxt);
+    ++tile_count;
+  }
+}
+
+// ------------------------------------------------------------- MMA issuer
+template <int L>
+__device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, uint32_t q_s,
+                        uint32_t slot_s, uint32_t p_s, uint32_t tmem, Misc& M, int* err) {
+  constexpr int NCH = LayoutT<L>::kChunks;
+  constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 64, false, false);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 64, true, true);
+  volatile int* abort_flag = &M.abort;
+
+  TileCursor cur = cursor_begin(p, sm);
+  int tile_count = 0, seg_count = 0;
+  while (cur.valid) {
+    const bool seg_first = cur.t == cur.t_lo;
+    const bool seg_last = cur.t + 1 == cur.t_hi;
+    if (seg_first) {
+      if (!mbar_wait(&M.q_full, seg_count & 1, abort_flag, err)) return;
+      ++seg_count;
+    }
+    // S^T[128 tok, 64 heads] = K_tile[128, d_qk] . Q^T  (K-major A and B)
+    for (int c = 0; c < NCH; ++c) {
+      if (!mbar_wait(&M.full[c], tile_count & 1, abort_flag, err)) return;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t ad = sdesc_sw128(slot_s + c * kSlotBytes + kk * 32, 16, 1024);
+        const uint64_t bd = sdesc_sw128(q_s + c * kQChunkBytes + kk * 32, 16, 1024);
+        umma_bf16_ss(tmem + kColS, ad, bd, idesc_qk, (c | kk) != 0);
+      }
+    }
+    umma_commit(&M.s_full);
+    if (seg_last) umma_commit(&M.q_empty);
+
+    // O^T[512 dims, 64 heads] += V^T[dims, 128 tok] . P^T[128 tok, heads]
+    if (!mbar_wait(&M.p_full, tile_count & 1, abort_flag, err)) return;
+    tc_fence_after();
+#pragma unroll 1
+    for (int m = 0; m < 4; ++m) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t ad = sdesc_sw128(slot_s + (2 * m) * kSlotBytes + kk * 2048, kSlotBytes, 1024);
+        const uint64_t bd = sdesc_sw128(p_s + kk * 2048, 8192, 1024);
+        umma_bf16_ss(tmem + kColO + 64 * m, ad, bd, idesc_pv, !(seg_first && kk == 0));
+      }
+      umma_commit(&M.empty[m]);
+    }
+    if (LayoutT<L>::kPInRopeSlot) umma_commit(&M.empty[4]);
+    if (seg_last) umma_commit(&M.o_full);
+    ++tile_count;
+    cur = cursor_next(p, sm, cur);
+  }
+}
+
+// ------------------------------------------------------------- softmax
+__device__ __forceinline__ void apply_sink(float sink, int lse_includes_sink, float& lse,
+                                           float& scale) {
+  // tests/reference.py:124-129
+  scale *= 1.0f / (1.0f + expf(sink - lse));
+  if (lse_includes_sink) {
+    const float m = fmaxf(lse, sink);
+    lse = m + logf(expf(lse - m) + expf(sink - m));
+  }
+}
+
+template <int L>
+__device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
+                            const int32_t* num_splits, float* lse_accum, float* o_accum,
+                            uint32_t p_s, uint32_t tmem, Misc& M, int* err) {
+  const int st = threadIdx.x - kProducerThreads;  // 0..127 = token row = TMEM lane
+  const int q = st >> 5, lane = st & 31;
+  const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+  const float scale_log2 = p.sm_scale * kLog2e;
+  volatile int* abort_flag = &M.abort;
+
+  TileCursor cur = cursor_begin(p, sm);
+  int tile_count = 0, seg_count = 0;
+  float m_run = -INFINITY;  // running max of head `st` (threads 0..63)
+  while (cur.valid) {
+    const bool seg_first = cur.t == cur.t_lo;
+    const bool seg_last = cur.t + 1 == cur.t_hi;
+    if (seg_first) m_run = -INFINITY;
+    const bool row_valid = st < tile_span(p, cur).npos;
+
+    if (!mbar_wait(&M.s_full, tile_count & 1, abort_flag, err)) return;
+    tc_fence_after();
+    // Column (per-head) max of this tile: S^T is read twice from TMEM (here
+    // and for P below) instead of being held in registers.
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float sv[32];
+      tmem_ld32(tl + kColS + 32 * hf, sv);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float mx = warp_max_f32(row_valid ? sv[j] * scale_log2 : -INFINITY);
+        if (lane == 0) M.red[q][32 * hf + j] = mx;
+      }
+    }
+    named_bar_sync(1, kSoftmaxThreads);
+    bool resc = false;
+    if (st < 64) {
+      const float mt = fmaxf(fmaxf(M.red[0][st], M.red[1][st]), fmaxf(M.red[2][st], M.red[3][st]));
+      const float m_old = m_run;
+      float m_new = m_old, alpha = 1.0f;
+      if (m_old == -INFINITY) {
+        m_new = mt;
+      } else if (mt > m_old + kRescaleThreshold) {
+        m_new = mt;
+        alpha = fast_exp2(m_old - m_new);
+        resc = true;
+      }
+      m_run = m_new;
+      M.m_use[st] = (m_new == -INFINITY) ? 0.0f : m_new;
+      M.alpha[st] = alpha;
+    }
+    const bool any_resc = named_bar_or(1, kSoftmaxThreads, resc);
+
+    // P = 2^(s - m) rounded to bf16 -> P^T row st in shared memory, and the
+    // per-lane partial row sums (TMEM columns kColL..) += the same bf16 P.
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float sv[32];
+      tmem_ld32(tl + kColS + 32 * hf, sv);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sv[j] = row_valid ? sv[j] * scale_log2 : -INFINITY;
+      uint32_t pk[16];
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        const float4 ma = *reinterpret_cast<const float4*>(&M.m_use[32 * hf + 8 * j4]);
+        const float4 mb = *reinterpret_cast<const float4*>(&M.m_use[32 * hf + 8 * j4 + 4]);
+        const float* sj = &sv[8 * j4];
+        pk[4 * j4 + 0] = pack_bf16(fast_exp2(sj[0] - ma.x), fast_exp2(sj[1] - ma.y));
+        pk[4 * j4 + 1] = pack_bf16(fast_exp2(sj[2] - ma.z), fast_exp2(sj[3] - ma.w));
+        pk[4 * j4 + 2] = pack_bf16(fast_exp2(sj[4] - mb.x), fast_exp2(sj[5] - mb.y));
+        pk[4 * j4 + 3] = pack_bf16(fast_exp2(sj[6] - mb.z), fast_exp2(sj[7] - mb.w));
+        sts_v4(p_s + sw128_off(st, 4 * hf + j4),
+               make_uint4(pk[4 * j4], pk[4 * j4 + 1], pk[4 * j4 + 2], pk[4 * j4 + 3]));
+      }
+      float lv[32];
+      if (!seg_first) {
+        tmem_ld32(tl + kColL + 32 * hf, lv);
+        tc_wait_ld();
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t w = pk[j];
+        const float p0 = __uint_as_float(w << 16), p1 = __uint_as_float(w & 0xFFFF0000u);
+        if (seg_first) {
+          lv[2 * j] = p0;
+          lv[2 * j + 1] = p1;
+        } else {
+          const float a0 = any_resc ? M.alpha[32 * hf + 2 * j] : 1.0f;
+          const float a1 = any_resc ? M.alpha[32 * hf + 2 * j + 1] : 1.0f;
+          lv[2 * j] = fmaf(lv[2 * j], a0, p0);
+          lv[2 * j + 1] = fmaf(lv[2 * j + 1], a1, p1);
+        }
+      }
+      tmem_st32(tl + kColL + 32 * hf, lv);
+    }
+    // Lazy O rescale (rare: only when some head's max rose by > 2^8).
+    if (any_resc && !seg_first) {
+      for (int m = 0; m < 4; ++m) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float ov[32];
+          tmem_ld32(tl + kColO + 64 * m + 32 * hf, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] *= M.alpha[32 * hf + j];
+          tmem_st32(tl + kColO + 64 * m + 32 * hf, ov);
+        }
+      }
+    }
+    tc_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(&M.p_full);
+
+    if (seg_last) {
+      // ---- epilogue of this (query row, split) ----
+      if (!mbar_wait(&M.o_full, seg_count & 1, abort_flag, err)) return;
+      tc_fence_after();
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float lv[32];
+        tmem_ld32(tl + kColL + 32 * hf, lv);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float v = warp_sum_f32(lv[j]);
+          if (lane == 0) M.red[q][32 * hf + j] = v;
+        }
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+      const bool final_out = (cur.t_lo == 0 && cur.t_hi == cur.ri.nt);
+      const int split = (cur.req == sm.begin_req_idx) ? sm.begin_split_idx : __ldg(num_splits + cur.req);
+      if (st < 64) {
+        const float l = (M.red[0][st] + M.red[1][st]) + (M.red[2][st] + M.red[3][st]);
+        const int head = g * kHeadsPerCta + st;
+        float lse = (m_run + log2f(l)) * kLn2;
+        float scale = 1.0f / l;
+        if (head < p.h_q) {
+          if (final_out) {
+            if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, scale);
+            p.lse[((int64_t)cur.ri.b * p.h_q + head) * p.s_q + cur.ri.s] = lse;
+          } else {
+            lse_accum[(int64_t)split * p.h_q + head] = lse;
+          }
+        } else {
+          scale = 0.0f;
+        }
+        M.scale_o[st] = scale;
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)cur.ri.b * p.stride_o_b +
+                           (int64_t)cur.ri.s * p.stride_o_s;
+      for (int m = 0; m < 4; ++m) {
+        const int dim = 128 * m + st;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float ov[32];
+          tmem_ld32(tl + kColO + 64 * m + 32 * hf, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int hl = 32 * hf + j;
+            const int head = g * kHeadsPerCta + hl;
+            if (head < p.h_q) {
+              const float v = ov[j] * M.scale_o[hl];
+              if (final_out)
+                out[(int64_t)head * p.stride_o_h + dim] = __float2bfloat16_rn(v);
+              else
+                o_accum[((int64_t)split * p.h_q + head) * kDv + dim] = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      ++seg_count;
+    }
+    ++tile_count;
+    cur = cursor_next(p, sm, cur);
+  }
+}
+
+template <int L>
+__global__ void __launch_bounds__(kThreads, 1)
+    sparse_decode_kernel(const dsv4b_decode_params p, const dsv4b_sched_meta* __restrict__ sched,
+                         const int32_t* __restrict__ num_splits, float* __restrict__ lse_accum,
+                         float* __restrict__ o_accum, int* __restrict__ err) {
+  using SP = SmemPlan<L>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_addr - raw_addr);
+  Misc& M = *reinterpret_cast<Misc*>(base + SP::kMiscOff);
+  const uint32_t q_s = base_addr + SP::kQOff;
+  const uint32_t slot_s = base_addr + SP::kSlotOff;
+  const uint32_t p_s = base_addr + SP::kPOff;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const dsv4b_sched_meta sm = sched[blockIdx.x];
+  const int g = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int c = 0; c < 9; ++c) mbar_init(&M.full[c], kProducerThreads);
+    for (int e = 0; e < 5; ++e) mbar_init(&M.empty[e], 1);
+    mbar_init(&M.s_full, 1);
+    mbar_init(&M.p_full, kSoftmaxThreads);
+    mbar_init(&M.q_full, kProducerThreads);
+    mbar_init(&M.q_empty, 1);
+    mbar_init(&M.o_full, 1);
+    M.abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&M.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = M.tmem_base;
+
+  if (warp < kProducerWarps) {
+    run_producer<L>(p, sm, g, q_s, slot_s, M, err);
+  } else if (warp < kMmaWarp) {
+    run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, p_s, tmem, M, err);
+  } else if (lane == 0) {
+    run_mma<L>(p, sm, q_s, slot_s, p_s, tmem, M, err);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int L>
+cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                               const int32_t* num_splits, int num_sm_parts, float* lse_accum,
+                               float* o_accum, int* err, cudaStream_t stream) {
+  constexpr int smem = SmemPlan<L>::kBytes;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
+    e = cudaFuncSetAttribute(sparse_decode_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_done[dev] = true;
+  }
+  const dim3 grid(num_sm_parts, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta);
+  sparse_decode_kernel<L><<<grid, kThreads, smem, stream>>>(p, sched, num_splits, lse_accum, o_accum, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                                 const int32_t* num_splits, int num_sm_parts, float* lse_accum,
+                                 float* o_accum, int* err, cudaStream_t stream) {
+  if (p.layout == DSV4B_LAYOUT_V32)
+    return launch_decode_impl<DSV4B_LAYOUT_V32>(p, sched, num_splits, num_sm_parts, lse_accum, o_accum,
+                                                err, stream);
+  return launch_decode_impl<DSV4B_LAYOUT_MODEL1>(p, sched, num_splits, num_sm_parts, lse_accum, o_accum,
+                                                 err, stream);
+}
+
+int decode_smem_bytes(int layout) {
+  return layout == DSV4B_LAYOUT_V32 ? SmemPlan<DSV4B_LAYOUT_V32>::kBytes
+                                    : SmemPlan<DSV4B_LAYOUT_MODEL1>::kBytes;
+}
+
+}  // namespace dsv4b

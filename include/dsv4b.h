@@ -1,0 +1,178 @@
+/*
+ * dsv4b.h - C ABI of the B200 (sm_100a) sparse FP8 MLA decode path.
+ *
+ * Plain C: pointers, sizes, int status codes.  No torch or C++ types.
+ * Every entry point runs asynchronously on the given CUDA stream (passed as
+ * void*, a cudaStream_t) and never synchronises the device.  All return
+ * DSV4B_OK (0) or a negative dsv4b_status; dsv4b_status_string() names it.
+ *
+ * Each declaration cites the reference interface it replaces
+ * (0xSero/deepseek-v4-flash-sm120, paths relative to that project).
+ */
+#ifndef DSV4B_H_
+#define DSV4B_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSV4B_API __attribute__((visibility("default")))
+#else
+#define DSV4B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference aborts the process on CUDA errors
+ * (csrc/common/defines.h:11-21) and raises TORCH_CHECK on bad arguments
+ * (csrc/api/sparse_decode.cpp:43-75); here both become return codes. */
+typedef enum dsv4b_status {
+  DSV4B_OK = 0,
+  DSV4B_ERR_INVALID_ARGUMENT = -1, /* shape / stride / pointer check failed */
+  DSV4B_ERR_UNSUPPORTED = -2,      /* valid request this build does not run */
+  DSV4B_ERR_CUDA = -3,             /* a CUDA runtime call failed */
+  DSV4B_ERR_WORKSPACE = -4,        /* workspace too small */
+  DSV4B_ERR_ARCH = -5,             /* device is not sm_100 */
+  DSV4B_ERR_KERNEL_TIMEOUT = -6    /* a kernel wait hit its time limit */
+} dsv4b_status;
+
+/* KV-cache byte layouts (csrc/common/params.h:12-15, ModelType). */
+typedef enum dsv4b_layout {
+  /* DeepSeek-V3.2: d_qk 576, d_v 512, 656 B/token, token-contiguous
+   * [512 x e4m3 | 4 x fp32 scale per 128 | 64 x bf16 RoPE]. */
+  DSV4B_LAYOUT_V32 = 0,
+  /* DeepSeek-V4-Flash: d_qk = d_v = 512; per page P x 576 B
+   * [448 x e4m3 | 64 x bf16 RoPE] rows, then P x 8 B UE8M0 scales
+   * (tests/reference.py:7-19). */
+  DSV4B_LAYOUT_MODEL1 = 1
+} dsv4b_layout;
+
+/* One record per SM part, 32 bytes, field order of the reference's
+ * DecodingSchedMeta (csrc/common/params.h:17-32).  Tiles are 128 top-k
+ * positions.  A part covers (begin_req_idx, begin_block_idx) up to
+ * (end_req_idx, end_block_idx) with the end tile exclusive; an empty part
+ * has end_req_idx < begin_req_idx.  "req" is a query row b * s_q + s. */
+typedef struct dsv4b_sched_meta {
+  int32_t begin_req_idx;
+  int32_t end_req_idx;
+  int32_t begin_block_idx;
+  int32_t end_block_idx;
+  int32_t begin_split_idx;
+  int32_t is_first_req_splitted;
+  int32_t is_last_req_splitted;
+  int32_t num_tiles;
+} dsv4b_sched_meta;
+
+/* Arguments of one decode call; mirrors SparseAttnDecodeParams
+ * (csrc/common/params.h:34-97) with 64-bit strides.  Element strides for
+ * q / out, byte strides for caches, element strides for indices. */
+typedef struct dsv4b_decode_params {
+  int32_t layout;            /* dsv4b_layout */
+  int32_t b, s_q, h_q, d_qk, d_v, topk;
+  float sm_scale;
+  int32_t lse_includes_sink; /* 1: lse = logaddexp(lse, sink) (reference
+                                tests/reference.py:124-129); 0: FlashMLA doc */
+
+  const void* q;             /* bf16 [b, s_q, h_q, d_qk], last dim contiguous */
+  int64_t stride_q_b, stride_q_s, stride_q_h;
+
+  const void* kv;            /* uint8/fp8 cache */
+  int32_t num_blocks, page_block_size;
+  int64_t stride_kv_block;   /* bytes between pages */
+  int64_t stride_kv_row;     /* bytes between tokens in a page (V32) */
+
+  const int32_t* indices;    /* [b, s_q, topk] flat page*P+offset, -1 = pad */
+  int64_t stride_idx_b, stride_idx_s;
+  const int32_t* topk_length;/* [b] or NULL */
+  const float* attn_sink;    /* [h_q] or NULL */
+
+  const void* extra_kv;      /* optional SWA sidecar cache, same layout */
+  int32_t extra_num_blocks, extra_page_block_size, extra_topk;
+  int64_t stride_extra_kv_block, stride_extra_kv_row;
+  const int32_t* extra_indices;     /* [b, s_q, extra_topk] */
+  int64_t stride_extra_idx_b, stride_extra_idx_s;
+  const int32_t* extra_topk_length; /* [b] or NULL */
+
+  void* out;                 /* bf16 [b, s_q, h_q, d_v] */
+  int64_t stride_o_b, stride_o_s, stride_o_h;
+  float* lse;                /* fp32 [b, h_q, s_q], contiguous */
+} dsv4b_decode_params;
+
+/* Library version (major*10000 + minor*100 + patch). */
+DSV4B_API int dsv4b_version(void);
+
+/* Human-readable name of a dsv4b_status. */
+DSV4B_API const char* dsv4b_status_string(int status);
+
+/* DSV4B_OK if `device` is an sm_100 part this build can run on.
+ * Replaces the Arch probe + SM_120 gate (csrc/common/params.h:100-116,
+ * csrc/api/sparse_decode.cpp:160-168). */
+DSV4B_API int dsv4b_check_device(int device);
+
+/* Number of SM parts (scheduler records) to use for h_q heads on `device`
+ * (148 SMs on B200; heads are processed in groups of 64).  Replaces the
+ * fixed num_sm_parts = 1 (csrc/api/sparse_decode.cpp:147-158). */
+DSV4B_API int dsv4b_num_sm_parts(int device, int h_q, int32_t* num_sm_parts);
+
+/* Bytes of device workspace a decode call needs (split-KV partials and
+ * the kernel status word); depends on shapes only. */
+DSV4B_API size_t dsv4b_workspace_bytes(int b, int s_q, int h_q, int num_sm_parts);
+
+/* get_mla_metadata: plan the split-KV tile schedule on the device from
+ * topk / topk_length / extra_topk_length (no host synchronisation, CUDA
+ * graph capturable).  Writes num_sm_parts records and num_splits
+ * [b*s_q + 1] (prefix offsets of each query row's splits).  Replaces the
+ * placeholder scheduler tensors of csrc/api/sparse_decode.cpp:147-158 and
+ * the FlashMLA get_mla_metadata protocol (flash_mla_interface.py:38-51). */
+DSV4B_API int dsv4b_get_mla_metadata(const dsv4b_decode_params* p, int num_sm_parts,
+                           dsv4b_sched_meta* sched_meta, int32_t* num_splits,
+                           void* stream);
+
+/* Sparse decode forward: decode kernel (K1) plus split combine (K3).
+ * Replaces dsv4_kernel::sparse_decode_fwd (csrc/api/sparse_decode.cpp:29-172)
+ * and sm120::launch_dsv4_sparse_decode_v32
+ * (csrc/sm120/decode/sparse_decode_instantiation.cu:10-23).  Writes
+ * p->out and p->lse ([b, h_q, s_q], so no transpose copy is needed). */
+DSV4B_API int dsv4b_sparse_decode(const dsv4b_decode_params* p,
+                        const dsv4b_sched_meta* sched_meta,
+                        const int32_t* num_splits, int num_sm_parts,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* The split-KV combine kernel alone (K3), for callers that run the decode
+ * kernel through dsv4b_sparse_decode_partial().  New: the reference has no
+ * combine (csrc/common/params.h:83-96 holds unused fields). */
+DSV4B_API int dsv4b_combine(const dsv4b_decode_params* p, const int32_t* num_splits,
+                  int num_sm_parts, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* The decode kernel alone (K1): rows whose work spans several parts leave
+ * fp32 partials in the workspace for dsv4b_combine().  Same inputs as
+ * dsv4b_sparse_decode. */
+DSV4B_API int dsv4b_sparse_decode_partial(const dsv4b_decode_params* p,
+                                const dsv4b_sched_meta* sched_meta,
+                                const int32_t* num_splits, int num_sm_parts,
+                                void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* Debug: gather + dequantise n rows (flat indices) of a cache into bf16
+ * [n, d_qk] with the decode kernel's own row decoder; -1 / out-of-range
+ * rows come out as zeros.  Mirrors load_kv_chunk
+ * (csrc/sm120/decode/sparse_decode_kernel.cuh:116-197) and the oracle
+ * unpack (tests/reference.py:45-79) for bit-exact checks. */
+DSV4B_API int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks,
+                         int page_block_size, int64_t stride_kv_block,
+                         int64_t stride_kv_row, const int32_t* indices, int n,
+                         void* out_bf16, void* stream);
+
+/* Reads (and clears) the kernel status word kept in the workspace into
+ * *flags (0 = no error).  Synchronises `stream`. */
+DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
+                             int* flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4B_H_ */

@@ -1,0 +1,280 @@
+"""GPU parity tests: the sm_100a path against the CPU oracle and against
+the reference's own golden vectors.  Tolerances (written here and in
+dsv4b_testutil): output max-abs 2e-2 at rtol 1e-2, LSE 1e-3; the gather /
+dequantisation is compared bit for bit."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from dsv4b_testutil import assert_matches, oracle_for
+from golden_io import golden_names, load_golden
+from oracle import schedule_oracle as SO
+from oracle import sparse_decode_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+
+def _kc():
+    from deepseek_v4_kernel import kvcache
+    return kvcache
+
+
+def _run(batch, topk_length=None, parts=None, extra=None, out=None):
+    from deepseek_v4_kernel import ops
+    q, kv, idx = batch.q, batch.kv, batch.indices
+    tsm = ns = None
+    if parts is not None:
+        b, s_q, h_q, d_qk = q.shape
+        o = torch.empty(b, s_q, h_q, 512, dtype=torch.bfloat16, device=q.device)
+        l = torch.empty(b, h_q, s_q, dtype=torch.float32, device=q.device)
+        p = ops.build_params(q, kv, idx, topk_length, batch.attn_sink,
+                             *(extra if extra else (None, None, None)), 512, batch.sm_scale, o, l)
+        tsm, ns = ops.get_mla_metadata_tensors(p, q.device, parts)
+    ekv, eidx, etk = extra if extra else (None, None, None)
+    return ops.sparse_decode_fwd(q, kv, idx, topk_length, batch.attn_sink, tsm, ns, ekv, eidx, etk,
+                                 512, batch.sm_scale, out=out)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    torch.cuda.set_device(0)
+    from deepseek_v4_kernel import _lib
+    assert _lib.lib.dsv4b_check_device(0) == 0, "not an sm_100 device"
+    yield
+    from deepseek_v4_kernel import ops
+    assert ops.read_kernel_status() == 0, "a kernel wait timed out"
+
+
+# ---------------------------------------------------------------- gather
+@pytest.mark.parametrize("layout", ["v32", "model1"])
+def test_gather_dequant_bit_exact(layout):
+    from deepseek_v4_kernel import ops
+    spec = _kc().BatchSpec(b=2, s_q=1, h_q=16, topk=300, ctx=2048, page_block=64, layout=layout,
+                           seed=11)
+    bt = _kc().make_batch(spec)
+    n_tok = bt.kv.shape[0] * bt.kv.shape[1]
+    idx = bt.indices.reshape(-1)[:512].clone()
+    idx[::17] = -1
+    idx[5] = n_tok
+    idx[9] = n_tok + 12345
+    got = ops.gather_dequant(bt.kv, idx)
+    kvn = bt.kv.cpu().view(torch.uint8).numpy()
+    if layout == "model1":
+        kvn = kvn.reshape(bt.kv.shape[0], -1)
+    want = O.gather_rows(layout, kvn, bt.kv.shape[1], idx.cpu().numpy())
+    got_bits = got.cpu().view(torch.int16).numpy().view(np.uint16)
+    want_bits = O.f32_to_bf16_bits(want)
+    assert np.array_equal(got_bits, want_bits)
+
+
+def test_gather_dequant_subnormal_and_extreme_scales():
+    """fp8 subnormals, UE8M0 exponents 0/1/254 (MODEL1), tiny / huge fp32
+    scales (V32) decode exactly like the oracle."""
+    from deepseek_v4_kernel import ops
+    rng = np.random.default_rng(3)
+    # V32: 8 tokens, one page
+    rec = rng.integers(0, 256, size=(8, 656), dtype=np.uint8)
+    rec[:, :512] &= 0xF7                      # clear bit 3 -> no NaN encodings (0x7F/0xFF)
+    rec[:, :64] = rng.integers(0, 8, size=(8, 64), dtype=np.uint8)  # subnormals
+    scales = np.array([[1e-30, 3e20, 1.0 / 3.0, 7.1e-3]] * 8, np.float32)
+    rec[:, 512:528] = scales.view(np.uint8)
+    rec[:, 528:] = rng.integers(0, 256, size=(8, 128), dtype=np.uint8) & 0x7F
+    kv = torch.from_numpy(rec).view(1, 8, 1, 656).cuda()
+    idx = torch.arange(8, dtype=torch.int32, device="cuda")
+    got = ops.gather_dequant(kv, idx).cpu().view(torch.int16).numpy().view(np.uint16)
+    want = O.f32_to_bf16_bits(O.gather_rows("v32", rec.reshape(1, 8, 1, 656), 8, np.arange(8)))
+    assert np.array_equal(got, want)
+    # MODEL1: 4 tokens, one page of 4
+    arena = np.zeros((1, 4 * 584), np.uint8)
+    nr = rng.integers(0, 256, size=(4, 576), dtype=np.uint8)
+    nr[:, :448] &= 0xF7
+    nr[:, 448:] &= 0x7F
+    arena[0, :4 * 576] = nr.reshape(-1)
+    sc = np.array([[0, 1, 254, 127, 120, 135, 2, 0]] * 4, np.uint8)
+    arena[0, 4 * 576:] = sc.reshape(-1)
+    kvm = torch.from_numpy(arena).view(1, 4, 1, 584).cuda()
+    got = ops.gather_dequant(kvm, torch.arange(4, dtype=torch.int32, device="cuda"))
+    got = got.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = O.f32_to_bf16_bits(O.gather_rows("model1", arena, 4, np.arange(4)))
+    assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------- golden (reference outputs)
+@pytest.mark.parametrize("name", golden_names())
+def test_matches_reference_golden(name):
+    from deepseek_v4_kernel import sparse_decode_fwd
+    g = load_golden(name)
+    P = g["page_block"]
+    q = torch.from_numpy(g["q_bf16"].view(np.int16)).view(torch.bfloat16).cuda()
+    kv = torch.from_numpy(g["kv_pages"]).cuda()
+    kv_view = kv.view(kv.shape[0], P, 1, 584)
+    idx = torch.from_numpy(g["indices"]).cuda()
+    tk = None if g["topk_length"] is None else torch.from_numpy(g["topk_length"]).cuda()
+    sink = None if g["attn_sink"] is None else torch.from_numpy(g["attn_sink"]).cuda()
+    out, lse, _, _ = sparse_decode_fwd(q, kv_view, idx, tk, sink, None, None, None, None, None,
+                                       512, g["sm_scale"])
+    assert_matches(out, lse, g["out_f32"], g["lse"])
+
+
+# ---------------------------------------------------------------- V32 vs oracle
+V32_CASES = [
+    # b, s_q, h_q, topk, ctx, page, invalid_tail, with_sink
+    (1, 1, 16, 128, 4096, 256, 16, True),
+    (2, 1, 64, 64, 512, 64, 0, False),
+    (2, 1, 64, 2048, 4096, 64, 0, True),
+    (2, 1, 128, 256, 1024, 64, 3, True),
+    (3, 2, 64, 300, 2048, 256, 7, True),       # s_q = 2, ragged topk
+    (1, 1, 32, 1, 64, 64, 0, True),            # topk = 1
+    (1, 1, 80, 200, 1000, 64, 0, False),       # h_q not a multiple of 64
+]
+
+
+@pytest.mark.parametrize("case", V32_CASES, ids=lambda c: "b{}s{}h{}k{}".format(*c[:4]))
+def test_v32_matches_oracle(case):
+    b, s_q, h_q, topk, ctx, page, tail, sink = case
+    spec = _kc().BatchSpec(b=b, s_q=s_q, h_q=h_q, topk=topk, ctx=ctx, page_block=page,
+                           invalid_tail=tail, with_sink=sink, seed=b * 131 + topk)
+    bt = _kc().make_batch(spec)
+    out, lse, _, _ = _run(bt)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink, bt.sm_scale, "v32")
+    assert_matches(out, lse, ref_out, ref_lse)
+
+
+def test_topk_length_and_zero_length():
+    spec = _kc().BatchSpec(b=4, s_q=1, h_q=64, topk=512, ctx=4096, page_block=64, seed=5)
+    bt = _kc().make_batch(spec)
+    tk = torch.tensor([64, 32, 0, 100000], dtype=torch.int32, device="cuda")
+    out, lse, _, _ = _run(bt, topk_length=tk)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, tk, bt.attn_sink, bt.sm_scale, "v32")
+    assert_matches(out, lse, ref_out, ref_lse)
+
+
+@pytest.mark.parametrize("parts", [1, 3, 7, 148, 300])
+def test_split_counts_agree(parts):
+    """Any scheduler part count gives the oracle's answer (split + combine)."""
+    spec = _kc().BatchSpec(b=3, s_q=1, h_q=64, topk=1000, ctx=8192, page_block=64,
+                           invalid_tail=5, seed=21)
+    bt = _kc().make_batch(spec)
+    tk = torch.tensor([1000, 130, 257], dtype=torch.int32, device="cuda")
+    out, lse, tsm, ns = _run(bt, topk_length=tk, parts=parts)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, tk, bt.attn_sink, bt.sm_scale, "v32")
+    assert_matches(out, lse, ref_out, ref_lse)
+    recs, want_ns = SO.plan(SO.row_tiles(3, 1, 1000, tk.tolist()), parts)
+    assert tsm.cpu().tolist() == recs
+    assert ns.cpu().tolist() == want_ns
+
+
+def test_extra_kv_sidecar():
+    kc = _kc()
+    spec = kc.BatchSpec(b=2, s_q=1, h_q=64, topk=256, ctx=2048, page_block=64, seed=8)
+    bt = kc.make_batch(spec)
+    ex = kc.make_batch(kc.BatchSpec(b=2, s_q=1, h_q=64, topk=192, ctx=512, page_block=64, seed=9))
+    etk = torch.tensor([192, 70], dtype=torch.int32, device="cuda")
+    extra = (ex.kv, ex.indices, etk)
+    out, lse, _, _ = _run(bt, extra=extra, parts=5)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink, bt.sm_scale, "v32",
+                                  extra=extra)
+    assert_matches(out, lse, ref_out, ref_lse)
+
+
+def test_model1_matches_oracle_multi_split():
+    spec = _kc().BatchSpec(b=2, s_q=2, h_q=128, topk=700, ctx=4096, page_block=64, layout="model1",
+                           invalid_tail=9, seed=4)
+    bt = _kc().make_batch(spec)
+    out, lse, _, _ = _run(bt, parts=11)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink, bt.sm_scale, "model1")
+    assert_matches(out, lse, ref_out, ref_lse)
+
+
+# ---------------------------------------------------------------- full size (config 1)
+def test_config1_full_size_properties():
+    """BASELINE config 1 at full size: rows checked against the oracle, and
+    size-independent properties (index order and -1 padding invariance)."""
+    kc = _kc()
+    bt = kc.make_batch(kc.CONFIGS[1])
+    out, lse, tsm, ns = _run(bt)
+    rows = [0, 17, 31]
+    ref_out, ref_lse = oracle_for(bt.q[rows], bt.kv, bt.indices[rows], None, bt.attn_sink,
+                                  bt.sm_scale, "v32")
+    assert_matches(out[rows], lse[rows], ref_out, ref_lse)
+    # permuting the top-k order changes nothing but summation order
+    perm = torch.randperm(bt.indices.shape[-1], device="cuda")
+    out2, lse2, _, _ = _run(kc.Batch(bt.q, bt.kv, bt.indices[..., perm].contiguous(), bt.attn_sink,
+                                     bt.sm_scale, bt.spec))
+    torch.testing.assert_close(out2.float(), out.float(), atol=2e-3, rtol=1e-2)
+    torch.testing.assert_close(lse2, lse, atol=1e-4, rtol=1e-4)
+    # appending -1 pads adds exactly one exp(0 - lse) term per pad to the LSE
+    pad = torch.full((32, 1, 128), -1, dtype=torch.int32, device="cuda")
+    idx3 = torch.cat([bt.indices, pad], dim=-1).contiguous()
+    _, lse3, _, _ = _run(kc.Batch(bt.q, bt.kv, idx3, None, bt.sm_scale, bt.spec))
+    _, lse_ns, _, _ = _run(kc.Batch(bt.q, bt.kv, bt.indices, None, bt.sm_scale, bt.spec))
+    want = torch.logaddexp(lse_ns, torch.full_like(lse_ns, math.log(128.0)))
+    torch.testing.assert_close(lse3, want, atol=2e-4, rtol=1e-4)
+
+
+# ---------------------------------------------------------------- graphs + interface
+def test_cuda_graph_replay():
+    from deepseek_v4_kernel import ops
+    kc = _kc()
+    bt = kc.make_batch(kc.BatchSpec(b=4, s_q=1, h_q=64, topk=2048, ctx=32768, page_block=256, seed=2))
+    out_ref, lse_ref, tsm, ns = _run(bt)
+    out = torch.empty_like(out_ref)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.sparse_decode_fwd(bt.q, bt.kv, bt.indices, None, bt.attn_sink, tsm, ns, None, None, None,
+                              512, bt.sm_scale, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        _, lse_g, _, _ = ops.sparse_decode_fwd(bt.q, bt.kv, bt.indices, None, bt.attn_sink, tsm, ns,
+                                               None, None, None, 512, bt.sm_scale, out=out)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, out_ref, atol=0, rtol=0)
+    torch.testing.assert_close(lse_g, lse_ref, atol=0, rtol=0)
+
+
+def test_flash_mla_interface_schedmeta_reuse():
+    import deepseek_v4_kernel as dk_
+    kc = _kc()
+    bt = kc.make_batch(kc.BatchSpec(b=2, s_q=1, h_q=64, topk=512, ctx=4096, page_block=64, seed=6))
+    meta, none = dk_.get_mla_metadata()
+    assert none is None and not meta.have_initialized
+    o1, l1 = dk_.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, meta, is_fp8_kvcache=True,
+                                        indices=bt.indices, attn_sink=bt.attn_sink)
+    assert meta.have_initialized and meta.config.topk == 512 and meta.tile_scheduler_metadata is not None
+    o2, l2 = dk_.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, meta, is_fp8_kvcache=True,
+                                        indices=bt.indices, attn_sink=bt.attn_sink)
+    torch.testing.assert_close(o1, o2, atol=0, rtol=0)
+    assert l1.shape == (2, 64, 1)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink,
+                                  1.0 / math.sqrt(576), "v32")
+    assert_matches(o1, l1, ref_out, ref_lse)
+
+
+def test_patch_wrapper_routes_sparse_to_b200():
+    from deepseek_v4_kernel import _patch, interface
+    import types
+    calls = []
+    fake = types.SimpleNamespace(FlashMLASchedMeta=interface.FlashMLASchedMeta)
+
+    def upstream(**kw):
+        calls.append(kw)
+        return "upstream"
+
+    fake.flash_mla_with_kvcache = upstream
+    assert _patch.patch_module(fake)
+    kc = _kc()
+    bt = kc.make_batch(kc.BatchSpec(b=1, s_q=1, h_q=64, topk=256, ctx=1024, page_block=64, seed=1))
+    meta = interface.FlashMLASchedMeta()
+    o, l = fake.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, meta, is_fp8_kvcache=True,
+                                       indices=bt.indices)
+    assert not calls and o.shape == (1, 1, 64, 512)
+    assert fake.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, meta, is_fp8_kvcache=False,
+                                       indices=None) == "upstream"
+    assert len(calls) == 1
