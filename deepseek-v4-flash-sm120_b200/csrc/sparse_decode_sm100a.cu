@@ -39,6 +39,8 @@
 // and the workspace status word records kErrWaitTimeout.
 #include <cuda_bf16.h>
 
+#include <cstddef>
+
 #include "dsv4b_internal.cuh"
 #include "dsv4b_kernels.h"
 
@@ -68,11 +70,15 @@ struct Misc {
   uint32_t tmem_base;
   int abort;
   int pad[2];
-  float red[4][64];
-  float m_use[64];
-  float alpha[64];
-  float scale_o[64];
+  alignas(16) float red[4][64];
+  alignas(16) float m_use[64];    // read as float4
+  alignas(16) float alpha[64];
+  alignas(16) float scale_o[64];
 };
+static_assert(offsetof(Misc, red) % 16 == 0 && offsetof(Misc, m_use) % 16 == 0 &&
+                  offsetof(Misc, alpha) % 16 == 0 && offsetof(Misc, scale_o) % 16 == 0,
+              "Misc float arrays must be 16-byte aligned (vector shared-memory loads)");
+static_assert(sizeof(Misc) % 16 == 0, "Misc size");
 
 template <int L>
 struct SmemPlan {
