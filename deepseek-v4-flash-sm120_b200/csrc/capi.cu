@@ -21,12 +21,16 @@ struct WsLayout {
   size_t lse_off, o_off, total;
 };
 
+// Workspace: [status word | lse_accum [splits][h_q] | o_accum [splits][head
+// groups][512 dims][64 heads]]; a query row split over k parts adds k - 1
+// splits, so b*s_q + parts bounds the split count.
 inline WsLayout ws_layout(int b, int s_q, int h_q, int parts) {
   const size_t max_splits = (size_t)b * s_q + (size_t)parts;
+  const size_t groups = ((size_t)h_q + dsv4b::kHeadsPerCtaPublic - 1) / dsv4b::kHeadsPerCtaPublic;
   WsLayout w;
   w.lse_off = kStatusBytes;
   w.o_off = align_up(w.lse_off + max_splits * h_q * sizeof(float), 256);
-  w.total = align_up(w.o_off + max_splits * h_q * 512 * sizeof(float), 256);
+  w.total = align_up(w.o_off + max_splits * groups * dsv4b::kHeadsPerCtaPublic * 512 * sizeof(float), 256);
   return w;
 }
 
@@ -56,7 +60,7 @@ int check_params(const dsv4b_decode_params* p) {
   if (!p->q || !p->indices || !p->out || !p->lse) return DSV4B_ERR_INVALID_ARGUMENT;
   if (!aligned(p->q, 16) || p->stride_q_b % 8 || p->stride_q_s % 8 || p->stride_q_h % 8)
     return DSV4B_ERR_INVALID_ARGUMENT;
-  if (!aligned(p->out, 8) || p->stride_o_b % 4 || p->stride_o_s % 4 || p->stride_o_h % 4)
+  if (!aligned(p->out, 16) || p->stride_o_b % 8 || p->stride_o_s % 8 || p->stride_o_h % 8)
     return DSV4B_ERR_INVALID_ARGUMENT;
   if (!aligned(p->lse, 4) || !aligned(p->indices, 4)) return DSV4B_ERR_INVALID_ARGUMENT;
   int rc = check_cache(p->layout, p->kv, p->num_blocks, p->page_block_size, p->stride_kv_block,

@@ -18,19 +18,14 @@ enum : int {
   kErrWaitTimeout = 1,   // an mbarrier wait ran past its time limit
 };
 
-// Wall-clock limit for any single mbarrier wait inside our kernels.  A
-// healthy wait is a few microseconds; this only fires if the pipeline is
-// broken, and lets the kernel leave instead of hanging the GPU.
-static constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
+// Limit for any single mbarrier wait inside our kernels, in SM cycles
+// (4e9 cycles = about 2 s at the 1.965 GHz B200 boost clock, longer at lower
+// clocks).  A healthy wait is microseconds; this only fires if the pipeline
+// is broken, and lets the kernel leave instead of hanging the GPU.
+static constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 
 // ------------------------------------------------------------- mbarrier
@@ -47,35 +42,38 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+// try_wait with a suspend-time hint: the thread sleeps in hardware until
+// the phase completes (or the hint, in ns, expires) instead of spinning and
+// taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity,
+                                              uint32_t suspend_ns = 1000000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
+      : "r"(bar_addr), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and
-// raises the CTA abort flag plus the global error word) if the limit is
-// reached or another role already aborted.
+// raises the CTA abort flag plus the global error word) once about
+// kWaitLimitCycles SM cycles have passed, or when another role already
+// aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* cta_abort, int* err_word) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  const long long t0 = clock64();
+  for (;;) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*cta_abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *cta_abort = 1;
-        if (err_word) atomicOr(err_word, kErrWaitTimeout);
-        return false;
-      }
+    if (*cta_abort) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *cta_abort = 1;
+      if (err_word) atomicOr(err_word, kErrWaitTimeout);
+      return false;
     }
   }
 }
@@ -140,6 +138,29 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 
@@ -211,6 +232,15 @@ __device__ __forceinline__ uint2 ldg_nc_v2(const void* p) {
                : "=r"(v.x), "=r"(v.y)
                : "l"(p));
   return v;
+}
+
+// 16-byte global -> shared async copy (LDGSTS); src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async_16(uint32_t saddr, const void* gptr, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(gptr), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void sts_v4(uint32_t saddr, uint4 v) {

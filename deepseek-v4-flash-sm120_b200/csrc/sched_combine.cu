@@ -11,8 +11,9 @@
 // runs on the device (one CTA), so a captured CUDA graph replays it.
 //
 // K3 merges splits: lse = log sum_i exp(lse_i), O = sum_i exp(lse_i - lse)
-// O_i, then the sink epilogue of tests/reference.py:124-129.  One warp per
-// (query row, head); rows with a single split were written by K1 directly.
+// O_i, then the sink epilogue of tests/reference.py:124-129.  One CTA per
+// (query row, 64-head group, 64-dim block); rows with a single split were
+// written by K1 directly.
 #include <cuda_bf16.h>
 
 #include "dsv4b_internal.cuh"
@@ -138,66 +139,76 @@ __global__ void __launch_bounds__(kSchedThreads)
 }
 
 // ------------------------------------------------------------- combine
-constexpr int kCombineWarps = 8;
+// One CTA per (query row, 64-head group, 64-dim block), one thread per
+// output dim.  The decode kernel leaves split partials dims-major:
+// o_accum[split][group][dim][64 heads] (already divided by the split's own
+// row sum) and lse_accum[split][h_q].
+constexpr int kCombineThreads = 64;
+constexpr int kCombineDimBlocks = kDv / kCombineThreads;  // 8
 
-__global__ void __launch_bounds__(kCombineWarps * 32)
+__global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const dsv4b_decode_params p, const int32_t* __restrict__ num_splits,
                    const float* __restrict__ lse_accum, const float* __restrict__ o_accum) {
-  const int r = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y * kCombineWarps + warp;
-  if (head >= p.h_q) return;
+  const int r = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
+  const int d = blockIdx.z * kCombineThreads + t;
   const int s0 = __ldg(num_splits + r), s1 = __ldg(num_splits + r + 1);
   const int n = s1 - s0;
   if (n <= 1) return;  // written by the decode kernel
-
-  float mx = -INFINITY;
-  for (int i = lane; i < n; i += 32) mx = fmaxf(mx, __ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.0f;
-  for (int i = lane; i < n; i += 32) sum += expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - mx);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  float lse = mx + logf(sum);
-
-  float4 acc[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = 0; i < n; ++i) {
-    const float w = expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - lse);
-    const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)(s0 + i) * p.h_q + head) * kDv);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4 v = __ldg(src + lane + 32 * k);
-      acc[k].x = fmaf(w, v.x, acc[k].x);
-      acc[k].y = fmaf(w, v.y, acc[k].y);
-      acc[k].z = fmaf(w, v.z, acc[k].z);
-      acc[k].w = fmaf(w, v.w, acc[k].w);
-    }
-  }
-  float scale = 1.0f;
-  if (p.attn_sink) {
-    const float sink = __ldg(p.attn_sink + head);
-    scale = 1.0f / (1.0f + expf(sink - lse));
-    if (p.lse_includes_sink) {
-      const float m = fmaxf(lse, sink);
-      lse = m + logf(expf(lse - m) + expf(sink - m));
-    }
-  }
+  const int n_groups = gridDim.y;
+  __shared__ float s_lse[kHeadsPerCta];
+  __shared__ float s_w[2][kHeadsPerCta];
+  __shared__ float s_scale[kHeadsPerCta];
   const int b = r / p.s_q, s = r - b * p.s_q;
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.stride_o_b +
-                       (int64_t)s * p.stride_o_s + (int64_t)head * p.stride_o_h;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[k].x * scale, acc[k].y * scale);
-    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc[k].z * scale, acc[k].w * scale);
-    uint2 v;
-    v.x = *reinterpret_cast<const uint32_t*>(&lo);
-    v.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(out + 4 * (lane + 32 * k)) = v;
+  {
+    const int head = g * kHeadsPerCta + t;
+    float lse = 0.0f, scale = 0.0f;
+    if (head < p.h_q) {
+      float mx = -INFINITY;
+      for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head));
+      float sum = 0.0f;
+      for (int i = 0; i < n; ++i) sum += expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - mx);
+      lse = mx + logf(sum);
+      float lse_out = lse;
+      scale = 1.0f;
+      if (p.attn_sink) {
+        const float sink = __ldg(p.attn_sink + head);
+        scale = 1.0f / (1.0f + expf(sink - lse));
+        if (p.lse_includes_sink) {
+          const float m = fmaxf(lse, sink);
+          lse_out = m + logf(expf(lse - m) + expf(sink - m));
+        }
+      }
+      if (blockIdx.z == 0) p.lse[((int64_t)b * p.h_q + head) * p.s_q + s] = lse_out;
+    }
+    s_lse[t] = lse;
+    s_scale[t] = scale;
   }
-  if (lane == 0) p.lse[((int64_t)b * p.h_q + head) * p.s_q + s] = lse;
+  __syncthreads();
+  float acc[kHeadsPerCta];
+#pragma unroll
+  for (int h = 0; h < kHeadsPerCta; ++h) acc[h] = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    const int head = g * kHeadsPerCta + t;
+    s_w[i & 1][t] = head < p.h_q ? expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - s_lse[t]) : 0.0f;
+    __syncthreads();
+    const float4* src = reinterpret_cast<const float4*>(
+        o_accum + (((int64_t)(s0 + i) * n_groups + g) * kDv + d) * kHeadsPerCta);
+#pragma unroll
+    for (int h4 = 0; h4 < kHeadsPerCta / 4; ++h4) {
+      const float4 v = __ldg(src + h4);
+      acc[4 * h4 + 0] = fmaf(s_w[i & 1][4 * h4 + 0], v.x, acc[4 * h4 + 0]);
+      acc[4 * h4 + 1] = fmaf(s_w[i & 1][4 * h4 + 1], v.y, acc[4 * h4 + 1]);
+      acc[4 * h4 + 2] = fmaf(s_w[i & 1][4 * h4 + 2], v.z, acc[4 * h4 + 2]);
+      acc[4 * h4 + 3] = fmaf(s_w[i & 1][4 * h4 + 3], v.w, acc[4 * h4 + 3]);
+    }
+  }
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.stride_o_b +
+                       (int64_t)s * p.stride_o_s + d;
+#pragma unroll
+  for (int h = 0; h < kHeadsPerCta; ++h) {
+    const int head = g * kHeadsPerCta + h;
+    if (head < p.h_q) out[(int64_t)head * p.stride_o_h] = __float2bfloat16_rn(acc[h] * s_scale[h]);
+  }
 }
 
 // ------------------------------------------------------------- debug gather
@@ -253,8 +264,8 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
 
 cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
                            const float* lse_accum, const float* o_accum, cudaStream_t stream) {
-  const dim3 grid(p.b * p.s_q, (p.h_q + kCombineWarps - 1) / kCombineWarps);
-  combine_kernel<<<grid, kCombineWarps * 32, 0, stream>>>(p, num_splits, lse_accum, o_accum);
+  const dim3 grid(p.b * p.s_q, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta, kCombineDimBlocks);
+  combine_kernel<<<grid, kCombineThreads, 0, stream>>>(p, num_splits, lse_accum, o_accum);
   return cudaGetLastError();
 }
 

@@ -46,6 +46,28 @@
 
 namespace dsv4b {
 
+#ifdef DSV4B_TRACE
+// Debug-build phase trace (never in the shipped library).  Each traced role
+// writes (clock64 | event | arg) words into the CTA's epilogue staging tile
+// (so no global memory traffic enters the pipeline; final-output epilogues
+// overwrite it, which the traced configurations do not use) and the log is
+// copied out at kernel end, read back with dsv4b_debug_trace_read().
+__device__ unsigned long long g_trace[4 * 3 * 128];
+__shared__ unsigned long long* s_trace_base;
+__shared__ int s_trace_n[3];
+#define DSV4B_TR_ROLE(role, ev, a)                                                        \
+  do {                                                                                    \
+    const int k_ = s_trace_n[role]++;                                                     \
+    if (k_ < 128)                                                                         \
+      s_trace_base[(role) * 128 + k_] =                                                   \
+          ((unsigned long long)clock64() << 24) | ((ev) << 16) | ((unsigned)(a) & 0xFFFFu); \
+  } while (0)
+#else
+#define DSV4B_TR_ROLE(role, ev, a) \
+  do {                             \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kProducerWarps = 8;
@@ -74,9 +96,11 @@ struct Misc {
   alignas(16) float m_use[64];    // read as float4
   alignas(16) float alpha[64];
   alignas(16) float scale_o[64];
+  alignas(16) __nv_bfloat16 stage[32][128];  // epilogue transpose tile (8 KB)
 };
 static_assert(offsetof(Misc, red) % 16 == 0 && offsetof(Misc, m_use) % 16 == 0 &&
-                  offsetof(Misc, alpha) % 16 == 0 && offsetof(Misc, scale_o) % 16 == 0,
+                  offsetof(Misc, alpha) % 16 == 0 && offsetof(Misc, scale_o) % 16 == 0 &&
+                  offsetof(Misc, stage) % 16 == 0,
               "Misc float arrays must be 16-byte aligned (vector shared-memory loads)");
 static_assert(sizeof(Misc) % 16 == 0, "Misc size");
 
@@ -115,43 +139,33 @@ __device__ __forceinline__ int empty_of(int c) {
 // ------------------------------------------------------------- producers
 template <int L>
 struct ProducerRegs {
-  // FP8 chunks 0-3 (A half of the tile), their scales, then the rest.
+  // FP8 chunks 0-3, their scales, then chunks 4.. and the RoPE chunk.
   uint4 a[8];
   uint4 sc;
   uint4 b[2 * (LayoutT<L>::kFp8Chunks - 4) + 4];
 };
 
+// Flat cache index of this thread's row in tile c, or -1 if the position
+// is padding (>= the row's attended length), which decodes to a zero row.
+__device__ __forceinline__ int producer_index(const dsv4b_decode_params& p, const TileCursor& c,
+                                              int row) {
+  const TileSpan ts = tile_span(p, c);
+  return row < ts.npos ? __ldg(ts.idx + row) : -1;
+}
+
 template <int L>
 __device__ __forceinline__ RowSrc producer_row(const dsv4b_decode_params& p, const TileCursor& c,
-                                               int row) {
+                                               int idx) {
   const TileSpan ts = tile_span(p, c);
-  const bool in_range = row < ts.npos;
-  const int idx = in_range ? __ldg(ts.idx + row) : -1;
-  return row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx, in_range);
+  return row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx, true);
 }
 
 template <int L>
-__device__ __forceinline__ void prefetch_row_l2(const RowSrc& r) {
-  if (!r.valid) return;
-  if constexpr (L == DSV4B_LAYOUT_V32) {
-    prefetch_l2_bulk(r.rec, LayoutT<L>::kRecordBytes);
-  } else {
-    prefetch_l2_bulk(r.rec, LayoutT<L>::kRowBytes);
-    prefetch_l2_bulk(reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(r.scl) & ~uintptr_t(15)),
-                     16);
-  }
-}
-
-template <int L>
-__device__ __forceinline__ void load_part_a(const RowSrc& r, int half, ProducerRegs<L>& R) {
+__device__ __forceinline__ void load_tile(const RowSrc& r, int half, ProducerRegs<L>& R) {
+  constexpr int nf = LayoutT<L>::kFp8Chunks;
 #pragma unroll
   for (int c = 0; c < 4; ++c) load_fp8_half<L>(r, c, half, R.a[2 * c], R.a[2 * c + 1]);
   R.sc = load_scales<L>(r);
-}
-
-template <int L>
-__device__ __forceinline__ void load_part_b(const RowSrc& r, int half, ProducerRegs<L>& R) {
-  constexpr int nf = LayoutT<L>::kFp8Chunks;
 #pragma unroll
   for (int c = 4; c < nf; ++c) load_fp8_half<L>(r, c, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1]);
   uint4 rope[4];
@@ -171,6 +185,11 @@ __device__ __forceinline__ void store_fp8_chunk(uint32_t slot, int row, int half
   sts_v4(slot + sw128_off(row, 4 * half + 3), o3);
 }
 
+// Producer loop.  Global loads of tile i+1 (and the index of tile i+2) are
+// issued as one batch right after the last chunk arrive of tile i: a proxy
+// fence followed by an mbarrier arrive waits for all of the thread's
+// outstanding loads, so no load may be in flight across a chunk hand-off.
+// The batch has the QK^T + softmax + first PV block of tile i to land.
 template <int L>
 __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                              uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
@@ -185,10 +204,8 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   TileCursor nxt = cursor_next(p, sm, cur);
 
   ProducerRegs<L> R;
-  RowSrc rs = producer_row<L>(p, cur, row);
-  if (half == 0) prefetch_row_l2<L>(rs);
-  load_part_a<L>(rs, half, R);
-  load_part_b<L>(rs, half, R);
+  load_tile<L>(producer_row<L>(p, cur, producer_index(p, cur, row)), half, R);
+  int idx_next = nxt.valid ? producer_index(p, nxt, row) : -1;
 
   int tile_count = 0, seg_count = 0;
   volatile int* abort_flag = &M.abort;
@@ -203,55 +220,46 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
         const int rem = i - j * (NCH * 8);
         const int c = rem >> 3, u = rem & 7;
         const int head = g * kHeadsPerCta + j;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (head < p.h_q) v = ldg_nc_v4(qb + (int64_t)head * p.stride_q_h + c * 64 + u * 8);
-        sts_v4(q_s + c * kQChunkBytes + sw128_off(j, u), v);
+        const bool ok = head < p.h_q;
+        cp_async_16(q_s + c * kQChunkBytes + sw128_off(j, u),
+                    qb + (ok ? (int64_t)head * p.stride_q_h + c * 64 + u * 8 : 0), ok ? 16u : 0u);
       }
+      cp_async_wait_all();
       fence_proxy_async_smem();
       mbar_arrive(&M.q_full);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 5, seg_count);
       ++seg_count;
     }
 
-    RowSrc rs_next;
-    rs_next.valid = false;
-    if (nxt.valid) {
-      rs_next = producer_row<L>(p, nxt, row);
-      if (half == 0) prefetch_row_l2<L>(rs_next);
-    }
-
-    const uint4 sc = R.sc;
+    if (ptid == 0) DSV4B_TR_ROLE(0, 1, tile_count);
     const uint32_t wait_par = (tile_count - 1) & 1;
-
-    // FP8 chunks 0..3 from R.a
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       if (tile_count > 0 && !mbar_wait(&M.empty[empty_of<L>(c)], wait_par, abort_flag, err)) return;
-      store_fp8_chunk(slot_s + c * kSlotBytes, row, half, R.a[2 * c], R.a[2 * c + 1],
-                      chunk_scale<L>(sc, c));
-      fence_proxy_async_smem();
-      mbar_arrive(&M.full[c]);
-    }
-    if (nxt.valid) load_part_a<L>(rs_next, half, R);
-
-    // FP8 chunks 4..NF-1 and the RoPE chunk from R.b
-#pragma unroll
-    for (int c = 4; c < NCH; ++c) {
-      if (tile_count > 0 && !mbar_wait(&M.empty[empty_of<L>(c)], wait_par, abort_flag, err)) return;
+      if (ptid == 0) DSV4B_TR_ROLE(0, 3, c);
       const uint32_t slot = slot_s + c * kSlotBytes;
-      if (c < NF) {
+      if (c < 4) {
+        store_fp8_chunk(slot, row, half, R.a[2 * c], R.a[2 * c + 1], chunk_scale<L>(R.sc, c));
+      } else if (c < NF) {
         store_fp8_chunk(slot, row, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1],
-                        chunk_scale<L>(sc, c));
+                        chunk_scale<L>(R.sc, c));
       } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i) sts_v4(slot + sw128_off(row, 4 * half + i), R.b[2 * (NF - 4) + i]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&M.full[c]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, c);
     }
-    if (nxt.valid) load_part_b<L>(rs_next, half, R);
+
+    // batch: data of the next tile, index of the one after
+    const TileCursor nn = cursor_next(p, sm, nxt);
+    if (nxt.valid) load_tile<L>(producer_row<L>(p, nxt, idx_next), half, R);
+    idx_next = nn.valid ? producer_index(p, nn, row) : -1;
+    if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
     cur = nxt;
-    nxt = cursor_next(p, sm, nxt);
+    nxt = nn;
     ++tile_count;
   }
 }
@@ -277,6 +285,7 @@ __device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm
     // S^T[128 tok, 64 heads] = K_tile[128, d_qk] . Q^T  (K-major A and B)
     for (int c = 0; c < NCH; ++c) {
       if (!mbar_wait(&M.full[c], tile_count & 1, abort_flag, err)) return;
+      DSV4B_TR_ROLE(1, 10, c);
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
@@ -286,10 +295,12 @@ __device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm
       }
     }
     umma_commit(&M.s_full);
+    DSV4B_TR_ROLE(1, 11, tile_count);
     if (seg_last) umma_commit(&M.q_empty);
 
     // O^T[512 dims, 64 heads] += V^T[dims, 128 tok] . P^T[128 tok, heads]
     if (!mbar_wait(&M.p_full, tile_count & 1, abort_flag, err)) return;
+    DSV4B_TR_ROLE(1, 12, tile_count);
     tc_fence_after();
 #pragma unroll 1
     for (int m = 0; m < 4; ++m) {
@@ -302,6 +313,7 @@ __device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm
       umma_commit(&M.empty[m]);
     }
     if (LayoutT<L>::kPInRopeSlot) umma_commit(&M.empty[4]);
+    DSV4B_TR_ROLE(1, 13, tile_count);
     if (seg_last) umma_commit(&M.o_full);
     ++tile_count;
     cur = cursor_next(p, sm, cur);
@@ -319,6 +331,97 @@ __device__ __forceinline__ void apply_sink(float sink, int lse_includes_sink, fl
   }
 }
 
+// Epilogue of one (query row, split): row sums, LSE (+ sink for a row
+// finished in this CTA), then either the bf16 output (whole row here) or
+// the fp32 split partial, dims-major [split][group][dim][64 heads].
+__device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm,
+                                         int g, const TileCursor& cur, float m_run,
+                                         const int32_t* num_splits, float* lse_accum, float* o_accum,
+                                         uint32_t tl, Misc& M) {
+  const int st = threadIdx.x - kProducerThreads;
+  const int q = st >> 5, lane = st & 31;
+#pragma unroll
+  for (int c16 = 0; c16 < 4; ++c16) {
+    float lv[16];
+    tmem_ld16(tl + kColL + 16 * c16, lv);
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float v = warp_sum_f32(lv[j]);
+      if (lane == 0) M.red[q][16 * c16 + j] = v;
+    }
+  }
+  named_bar_sync(1, kSoftmaxThreads);
+  const bool final_out = (cur.t_lo == 0 && cur.t_hi == cur.ri.nt);
+  const int split = (cur.req == sm.begin_req_idx) ? sm.begin_split_idx : __ldg(num_splits + cur.req);
+  if (st < 64) {
+    const float l = (M.red[0][st] + M.red[1][st]) + (M.red[2][st] + M.red[3][st]);
+    const int head = g * kHeadsPerCta + st;
+    float lse = (m_run + log2f(l)) * kLn2;
+    float scale = 1.0f / l;
+    if (head < p.h_q) {
+      if (final_out) {
+        if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, scale);
+        p.lse[((int64_t)cur.ri.b * p.h_q + head) * p.s_q + cur.ri.s] = lse;
+      } else {
+        lse_accum[(int64_t)split * p.h_q + head] = lse;
+      }
+    } else {
+      scale = 0.0f;
+    }
+    M.scale_o[st] = scale;
+  }
+  named_bar_sync(1, kSoftmaxThreads);
+  if (final_out) {
+    // bf16 [heads, dims] through a 32-head x 128-dim staging tile so the
+    // global stores are 16-byte and contiguous along dims.
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)cur.ri.b * p.stride_o_b +
+                         (int64_t)cur.ri.s * p.stride_o_s;
+    const int r = st >> 2, part = st & 3;
+#pragma unroll 1
+    for (int mh = 0; mh < 8; ++mh) {  // 4 M-blocks x 2 head halves
+      const int m = mh >> 1, hf = mh & 1;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float ov[16];
+        tmem_ld16(tl + kColO + 64 * m + 32 * hf + 16 * c, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          M.stage[16 * c + j][st] = __float2bfloat16_rn(ov[j] * M.scale_o[32 * hf + 16 * c + j]);
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+      const int head = g * kHeadsPerCta + 32 * hf + r;
+      if (head < p.h_q) {
+        uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)head * p.stride_o_h + 128 * m + 32 * part);
+        const uint4* src = reinterpret_cast<const uint4*>(&M.stage[r][32 * part]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = src[k];
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+    }
+  } else {
+    const int n_groups = (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta;
+#pragma unroll 1
+    for (int m = 0; m < 4; ++m) {
+      float4* dst = reinterpret_cast<float4*>(
+          o_accum + (((int64_t)split * n_groups + g) * kDv + 128 * m + st) * kHeadsPerCta);
+#pragma unroll
+      for (int c16 = 0; c16 < 4; ++c16) {
+        float ov[16];
+        tmem_ld16(tl + kColO + 64 * m + 16 * c16, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 sc = *reinterpret_cast<const float4*>(&M.scale_o[16 * c16 + 4 * j4]);
+          dst[4 * c16 + j4] = make_float4(ov[4 * j4] * sc.x, ov[4 * j4 + 1] * sc.y,
+                                          ov[4 * j4 + 2] * sc.z, ov[4 * j4 + 3] * sc.w);
+        }
+      }
+    }
+  }
+}
+
 template <int L>
 __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                             const int32_t* num_splits, float* lse_accum, float* o_accum,
@@ -331,169 +434,135 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
 
   TileCursor cur = cursor_begin(p, sm);
   int tile_count = 0, seg_count = 0;
-  float m_run = -INFINITY;  // running max of head `st` (threads 0..63)
+  float m_run = -INFINITY;  // stabiliser of head `st` (threads 0..63), log2 units
   while (cur.valid) {
     const bool seg_first = cur.t == cur.t_lo;
     const bool seg_last = cur.t + 1 == cur.t_hi;
     if (seg_first) m_run = -INFINITY;
-    const bool row_valid = st < tile_span(p, cur).npos;
+    const float row_scale = st < tile_span(p, cur).npos ? scale_log2 : 0.0f;  // 0 marks padding rows
 
     if (!mbar_wait(&M.s_full, tile_count & 1, abort_flag, err)) return;
+    if (st == 0) DSV4B_TR_ROLE(2, 20, tile_count);
     tc_fence_after();
-    // Column (per-head) max of this tile: S^T is read twice from TMEM (here
-    // and for P below) instead of being held in registers.
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      float sv[32];
-      tmem_ld32(tl + kColS + 32 * hf, sv);
-      tc_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float mx = warp_max_f32(row_valid ? sv[j] * scale_log2 : -INFINITY);
-        if (lane == 0) M.red[q][32 * hf + j] = mx;
-      }
-    }
-    named_bar_sync(1, kSoftmaxThreads);
-    bool resc = false;
-    if (st < 64) {
-      const float mt = fmaxf(fmaxf(M.red[0][st], M.red[1][st]), fmaxf(M.red[2][st], M.red[3][st]));
-      const float m_old = m_run;
-      float m_new = m_old, alpha = 1.0f;
-      if (m_old == -INFINITY) {
-        m_new = mt;
-      } else if (mt > m_old + kRescaleThreshold) {
-        m_new = mt;
-        alpha = fast_exp2(m_old - m_new);
-        resc = true;
-      }
-      m_run = m_new;
-      M.m_use[st] = (m_new == -INFINITY) ? 0.0f : m_new;
-      M.alpha[st] = alpha;
-    }
-    const bool any_resc = named_bar_or(1, kSoftmaxThreads, resc);
 
-    // P = 2^(s - m) rounded to bf16 -> P^T row st in shared memory, and the
-    // per-lane partial row sums (TMEM columns kColL..) += the same bf16 P.
+    // Phase 1.  After a row's first tile the stabiliser m_use is kept unless
+    // some logit exceeds it by more than 2^8: one vote instead of a
+    // cross-warp max exchange per tile.
+    bool need = seg_first;
+    if (!seg_first && row_scale != 0.0f) {
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      float sv[32];
-      tmem_ld32(tl + kColS + 32 * hf, sv);
+      for (int c16 = 0; c16 < 4; ++c16) {
+        float sv[16];
+        tmem_ld16(tl + kColS + 16 * c16, sv);
+        tc_wait_ld();
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
+          need |= (sv[4 * j4] * row_scale > mu.x + kRescaleThreshold) |
+                  (sv[4 * j4 + 1] * row_scale > mu.y + kRescaleThreshold) |
+                  (sv[4 * j4 + 2] * row_scale > mu.z + kRescaleThreshold) |
+                  (sv[4 * j4 + 3] * row_scale > mu.w + kRescaleThreshold);
+        }
+      }
+    }
+    bool any_resc = false;
+    if (named_bar_or(1, kSoftmaxThreads, need)) {
+      // Column (per-head) max of the tile via redux.sync + a 4-warp exchange.
+#pragma unroll
+      for (int c16 = 0; c16 < 4; ++c16) {
+        float sv[16];
+        tmem_ld16(tl + kColS + 16 * c16, sv);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float mx = warp_max_f32(row_scale != 0.0f ? sv[j] * row_scale : -INFINITY);
+          if (lane == 0) M.red[q][16 * c16 + j] = mx;
+        }
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+      bool resc = false;
+      if (st < 64) {
+        const float mt = fmaxf(fmaxf(M.red[0][st], M.red[1][st]), fmaxf(M.red[2][st], M.red[3][st]));
+        const float m_old = m_run;
+        float m_new = m_old, alpha = 1.0f;
+        if (m_old == -INFINITY) {
+          m_new = mt;
+        } else if (mt > m_old + kRescaleThreshold) {
+          m_new = mt;
+          alpha = fast_exp2(m_old - m_new);
+          resc = true;
+        }
+        m_run = m_new;
+        M.m_use[st] = (m_new == -INFINITY) ? 0.0f : m_new;
+        M.alpha[st] = alpha;
+      }
+      any_resc = named_bar_or(1, kSoftmaxThreads, resc);
+    }
+    if (st == 0) DSV4B_TR_ROLE(2, 21, any_resc);
+
+    // Phase 2.  P = 2^(s - m) rounded to bf16 -> P^T row st in shared
+    // memory; per-lane partial row sums (TMEM columns kColL..) += same P.
+#pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float sv[16];
+      tmem_ld16(tl + kColS + 16 * c16, sv);
+      float lv[16];
+      if (!seg_first) tmem_ld16(tl + kColL + 16 * c16, lv);
       tc_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sv[j] = row_valid ? sv[j] * scale_log2 : -INFINITY;
-      uint32_t pk[16];
+      uint32_t pk[8];
 #pragma unroll
       for (int j4 = 0; j4 < 4; ++j4) {
-        const float4 ma = *reinterpret_cast<const float4*>(&M.m_use[32 * hf + 8 * j4]);
-        const float4 mb = *reinterpret_cast<const float4*>(&M.m_use[32 * hf + 8 * j4 + 4]);
-        const float* sj = &sv[8 * j4];
-        pk[4 * j4 + 0] = pack_bf16(fast_exp2(sj[0] - ma.x), fast_exp2(sj[1] - ma.y));
-        pk[4 * j4 + 1] = pack_bf16(fast_exp2(sj[2] - ma.z), fast_exp2(sj[3] - ma.w));
-        pk[4 * j4 + 2] = pack_bf16(fast_exp2(sj[4] - mb.x), fast_exp2(sj[5] - mb.y));
-        pk[4 * j4 + 3] = pack_bf16(fast_exp2(sj[6] - mb.z), fast_exp2(sj[7] - mb.w));
-        sts_v4(p_s + sw128_off(st, 4 * hf + j4),
-               make_uint4(pk[4 * j4], pk[4 * j4 + 1], pk[4 * j4 + 2], pk[4 * j4 + 3]));
+        const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
+        const float e0 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 0], row_scale, -mu.x)) : 0.0f;
+        const float e1 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 1], row_scale, -mu.y)) : 0.0f;
+        const float e2 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 2], row_scale, -mu.z)) : 0.0f;
+        const float e3 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 3], row_scale, -mu.w)) : 0.0f;
+        pk[2 * j4] = pack_bf16(e0, e1);
+        pk[2 * j4 + 1] = pack_bf16(e2, e3);
       }
-      float lv[32];
-      if (!seg_first) {
-        tmem_ld32(tl + kColL + 32 * hf, lv);
-        tc_wait_ld();
-      }
+      sts_v4(p_s + sw128_off(st, 2 * c16), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+      sts_v4(p_s + sw128_off(st, 2 * c16 + 1), make_uint4(pk[4], pk[5], pk[6], pk[7]));
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const uint32_t w = pk[j];
-        const float p0 = __uint_as_float(w << 16), p1 = __uint_as_float(w & 0xFFFF0000u);
+      for (int j = 0; j < 8; ++j) {
+        const float p0 = __uint_as_float(pk[j] << 16), p1 = __uint_as_float(pk[j] & 0xFFFF0000u);
         if (seg_first) {
           lv[2 * j] = p0;
           lv[2 * j + 1] = p1;
         } else {
-          const float a0 = any_resc ? M.alpha[32 * hf + 2 * j] : 1.0f;
-          const float a1 = any_resc ? M.alpha[32 * hf + 2 * j + 1] : 1.0f;
+          const float a0 = any_resc ? M.alpha[16 * c16 + 2 * j] : 1.0f;
+          const float a1 = any_resc ? M.alpha[16 * c16 + 2 * j + 1] : 1.0f;
           lv[2 * j] = fmaf(lv[2 * j], a0, p0);
           lv[2 * j + 1] = fmaf(lv[2 * j + 1], a1, p1);
         }
       }
-      tmem_st32(tl + kColL + 32 * hf, lv);
+      tmem_st16(tl + kColL + 16 * c16, lv);
     }
-    // Lazy O rescale (rare: only when some head's max rose by > 2^8).
+    // Lazy O rescale (only when some head's max rose by more than 2^8).
     if (any_resc && !seg_first) {
-      for (int m = 0; m < 4; ++m) {
+#pragma unroll 1
+      for (int cc = 0; cc < 16; ++cc) {  // 4 M-blocks x 4 column groups
+        const uint32_t col = kColO + 64 * (cc >> 2) + 16 * (cc & 3);
+        float ov[16];
+        tmem_ld16(tl + col, ov);
+        tc_wait_ld();
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float ov[32];
-          tmem_ld32(tl + kColO + 64 * m + 32 * hf, ov);
-          tc_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) ov[j] *= M.alpha[32 * hf + j];
-          tmem_st32(tl + kColO + 64 * m + 32 * hf, ov);
-        }
+        for (int j = 0; j < 16; ++j) ov[j] *= M.alpha[16 * (cc & 3) + j];
+        tmem_st16(tl + col, ov);
       }
     }
     tc_wait_st();
     fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(&M.p_full);
+    if (st == 0) DSV4B_TR_ROLE(2, 23, tile_count);
 
     if (seg_last) {
-      // ---- epilogue of this (query row, split) ----
       if (!mbar_wait(&M.o_full, seg_count & 1, abort_flag, err)) return;
+      if (st == 0) DSV4B_TR_ROLE(2, 24, seg_count);
       tc_fence_after();
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float lv[32];
-        tmem_ld32(tl + kColL + 32 * hf, lv);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = warp_sum_f32(lv[j]);
-          if (lane == 0) M.red[q][32 * hf + j] = v;
-        }
-      }
-      named_bar_sync(1, kSoftmaxThreads);
-      const bool final_out = (cur.t_lo == 0 && cur.t_hi == cur.ri.nt);
-      const int split = (cur.req == sm.begin_req_idx) ? sm.begin_split_idx : __ldg(num_splits + cur.req);
-      if (st < 64) {
-        const float l = (M.red[0][st] + M.red[1][st]) + (M.red[2][st] + M.red[3][st]);
-        const int head = g * kHeadsPerCta + st;
-        float lse = (m_run + log2f(l)) * kLn2;
-        float scale = 1.0f / l;
-        if (head < p.h_q) {
-          if (final_out) {
-            if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, scale);
-            p.lse[((int64_t)cur.ri.b * p.h_q + head) * p.s_q + cur.ri.s] = lse;
-          } else {
-            lse_accum[(int64_t)split * p.h_q + head] = lse;
-          }
-        } else {
-          scale = 0.0f;
-        }
-        M.scale_o[st] = scale;
-      }
-      named_bar_sync(1, kSoftmaxThreads);
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)cur.ri.b * p.stride_o_b +
-                           (int64_t)cur.ri.s * p.stride_o_s;
-      for (int m = 0; m < 4; ++m) {
-        const int dim = 128 * m + st;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float ov[32];
-          tmem_ld32(tl + kColO + 64 * m + 32 * hf, ov);
-          tc_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int hl = 32 * hf + j;
-            const int head = g * kHeadsPerCta + hl;
-            if (head < p.h_q) {
-              const float v = ov[j] * M.scale_o[hl];
-              if (final_out)
-                out[(int64_t)head * p.stride_o_h + dim] = __float2bfloat16_rn(v);
-              else
-                o_accum[((int64_t)split * p.h_q + head) * kDv + dim] = v;
-            }
-          }
-        }
-      }
+      epilogue(p, sm, g, cur, m_run, num_splits, lse_accum, o_accum, tl, M);
       tc_fence_before();
+      if (st == 0) DSV4B_TR_ROLE(2, 25, seg_count);
       ++seg_count;
     }
     ++tile_count;
@@ -529,6 +598,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&M.q_empty, 1);
     mbar_init(&M.o_full, 1);
     M.abort = 0;
+#ifdef DSV4B_TRACE
+    s_trace_n[0] = s_trace_n[1] = s_trace_n[2] = 0;
+    s_trace_base = reinterpret_cast<unsigned long long*>(&M.stage[0][0]);
+    for (int i = 0; i < 3 * 128; ++i) s_trace_base[i] = 0;
+#endif
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
@@ -554,6 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+#ifdef DSV4B_TRACE
+  if (blockIdx.x < 4 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < 3 * 128; i += blockDim.x) g_trace[blockIdx.x * 3 * 128 + i] = s_trace_base[i];
+#endif
 }
 
 template <int L>
@@ -587,6 +665,14 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
   return launch_decode_impl<DSV4B_LAYOUT_MODEL1>(p, sched, num_splits, num_sm_parts, lse_accum, o_accum,
                                                  err, stream);
 }
+
+#ifdef DSV4B_TRACE
+extern "C" DSV4B_API int dsv4b_debug_trace_read(unsigned long long* dst, int max_words) {
+  const int n = 4 * 3 * 128 < max_words ? 4 * 3 * 128 : max_words;
+  cudaMemcpyFromSymbol(dst, g_trace, n * sizeof(unsigned long long));
+  return n;
+}
+#endif
 
 int decode_smem_bytes(int layout) {
   return layout == DSV4B_LAYOUT_V32 ? SmemPlan<DSV4B_LAYOUT_V32>::kBytes
