@@ -448,8 +448,10 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     // Phase 1.  After a row's first tile the stabiliser m_use is kept unless
     // some logit exceeds it by more than 2^8: one vote instead of a
     // cross-warp max exchange per tile.
+    // (tcgen05.ld / wait::ld are .sync.aligned: every lane must execute
+    // them, padding rows included, so only the compare is masked.)
     bool need = seg_first;
-    if (!seg_first && row_scale != 0.0f) {
+    if (!seg_first) {
 #pragma unroll
       for (int c16 = 0; c16 < 4; ++c16) {
         float sv[16];
@@ -458,10 +460,10 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
 #pragma unroll
         for (int j4 = 0; j4 < 4; ++j4) {
           const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
-          need |= (sv[4 * j4] * row_scale > mu.x + kRescaleThreshold) |
-                  (sv[4 * j4 + 1] * row_scale > mu.y + kRescaleThreshold) |
-                  (sv[4 * j4 + 2] * row_scale > mu.z + kRescaleThreshold) |
-                  (sv[4 * j4 + 3] * row_scale > mu.w + kRescaleThreshold);
+          need |= (row_scale != 0.0f) & ((sv[4 * j4] * row_scale > mu.x + kRescaleThreshold) |
+                                         (sv[4 * j4 + 1] * row_scale > mu.y + kRescaleThreshold) |
+                                         (sv[4 * j4 + 2] * row_scale > mu.z + kRescaleThreshold) |
+                                         (sv[4 * j4 + 3] * row_scale > mu.w + kRescaleThreshold));
         }
       }
     }
