@@ -221,14 +221,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
 // ------------------------------------------------------------- memory
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint2 ldg_nc_v2(const void* p) {
   uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+  asm volatile("ld.global.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
                : "=r"(v.x), "=r"(v.y)
                : "l"(p));
   return v;

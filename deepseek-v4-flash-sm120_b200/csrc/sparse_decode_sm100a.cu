@@ -91,7 +91,8 @@ struct Misc {
   uint64_t s_full, p_full, q_full, q_empty, o_full;
   uint32_t tmem_base;
   int abort;
-  int pad[2];
+  uint32_t sink_word;  // target of the producers' load-completion fold
+  int pad[1];
   alignas(16) float red[4][64];
   alignas(16) float m_use[64];    // read as float4
   alignas(16) float alpha[64];
@@ -137,75 +138,161 @@ __device__ __forceinline__ int empty_of(int c) {
 }
 
 // ------------------------------------------------------------- producers
+// Gather mapping.  Producer warp w owns tile rows 16w..16w+15 and handles
+// four of them per pass: in pass k lane l works on row 16w + 4k + (l >> 3)
+// and on the 16-byte column q = l & 7 of a 128-byte block of that row.  A
+// warp load instruction therefore reads four rows x 128 contiguous bytes
+// (whole 32-byte sectors), and the unit of work is a "chunk pair": 128
+// columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
+// pair one PV M-block releases.
+//
+// Loads are split in two register phases per tile.  Phase A (pairs 0-1 and
+// the scales) is issued at the end of the previous tile together with an
+// L2 bulk prefetch of each whole row, and landed there.  Phase B (pairs 2-3
+// and MODEL1 RoPE) is issued after pairs 0-1 are stored and hits L2; the
+// V32 RoPE chunk is loaded after pair 3, while waiting for the previous PV.  A proxy fence
+// followed by an mbarrier arrive waits for all of the thread's outstanding
+// loads, so every hand-off happens with no load in flight.
+constexpr int kRowsPerThread = 4;
+
 template <int L>
-struct ProducerRegs {
-  // FP8 chunks 0-3, their scales, then chunks 4.. and the RoPE chunk.
-  uint4 a[8];
-  uint4 sc;
-  uint4 b[2 * (LayoutT<L>::kFp8Chunks - 4) + 4];
+struct ProdRegs {
+  RowSrc rs[kRowsPerThread];
+  uint4 fa[2][kRowsPerThread];  // phase A: pairs 0, 1
+  uint4 sc[kRowsPerThread];     // V32: 4 fp32 scales; MODEL1: 8 UE8M0 bytes in .x/.y
+  uint4 fb[2][kRowsPerThread];  // phase B: pairs 2, 3 (MODEL1 pair 3: fp8 or RoPE part 0)
+  uint4 rp[kRowsPerThread];     // V32 RoPE; MODEL1 RoPE part 1
 };
 
-// Flat cache index of this thread's row in tile c, or -1 if the position
-// is padding (>= the row's attended length), which decodes to a zero row.
+// Flat cache index of tile row r, or -1 for padding (>= the row's attended
+// length), which decodes to a zero row.
 __device__ __forceinline__ int producer_index(const dsv4b_decode_params& p, const TileCursor& c,
-                                              int row) {
+                                              int r) {
   const TileSpan ts = tile_span(p, c);
-  return row < ts.npos ? __ldg(ts.idx + row) : -1;
+  return r < ts.npos ? __ldg(ts.idx + r) : -1;
+}
+
+__device__ __forceinline__ uint4 ldg_or_zero(bool ok, const uint8_t* ptr) {
+  return ok ? ldg_nc_v4(ptr) : make_uint4(0, 0, 0, 0);
 }
 
 template <int L>
-__device__ __forceinline__ RowSrc producer_row(const dsv4b_decode_params& p, const TileCursor& c,
-                                               int idx) {
+__device__ __forceinline__ void rows_of(const dsv4b_decode_params& p, const TileCursor& c,
+                                        const int (&idx)[kRowsPerThread], ProdRegs<L>& R) {
   const TileSpan ts = tile_span(p, c);
-  return row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx, true);
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k)
+    R.rs[k] = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
 }
 
 template <int L>
-__device__ __forceinline__ void load_tile(const RowSrc& r, int half, ProducerRegs<L>& R) {
-  constexpr int nf = LayoutT<L>::kFp8Chunks;
+__device__ __forceinline__ void load_phase_a(int q, ProdRegs<L>& R) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) load_fp8_half<L>(r, c, half, R.a[2 * c], R.a[2 * c + 1]);
-  R.sc = load_scales<L>(r);
-#pragma unroll
-  for (int c = 4; c < nf; ++c) load_fp8_half<L>(r, c, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1]);
-  uint4 rope[4];
-  load_rope_half<L>(r, half, rope);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) R.b[2 * (nf - 4) + i] = rope[i];
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    const RowSrc& r = R.rs[k];
+    R.fa[0][k] = ldg_or_zero(r.valid, r.rec + 16 * q);
+    R.fa[1][k] = ldg_or_zero(r.valid, r.rec + 128 + 16 * q);
+    R.sc[k] = load_scales<L>(r);
+  }
 }
 
-__device__ __forceinline__ void store_fp8_chunk(uint32_t slot, int row, int half, uint4 a, uint4 b,
-                                                float s) {
-  uint4 o0, o1, o2, o3;
-  dq16(a, s, o0, o1);
-  dq16(b, s, o2, o3);
-  sts_v4(slot + sw128_off(row, 4 * half + 0), o0);
-  sts_v4(slot + sw128_off(row, 4 * half + 1), o1);
-  sts_v4(slot + sw128_off(row, 4 * half + 2), o2);
-  sts_v4(slot + sw128_off(row, 4 * half + 3), o3);
+template <int L>
+__device__ __forceinline__ void prefetch_rows_l2(int q, const ProdRegs<L>& R) {
+  if (q != 0) return;
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    const RowSrc& r = R.rs[k];
+    if (!r.valid) continue;
+    if constexpr (L == DSV4B_LAYOUT_V32) {
+      prefetch_l2_bulk(r.rec, LayoutT<L>::kRecordBytes);
+    } else {
+      prefetch_l2_bulk(r.rec, LayoutT<L>::kRowBytes);
+      prefetch_l2_bulk(reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(r.scl) & ~uintptr_t(15)), 16);
+    }
+  }
 }
 
-// Producer loop.  Global loads of tile i+1 (and the index of tile i+2) are
-// issued as one batch right after the last chunk arrive of tile i: a proxy
-// fence followed by an mbarrier arrive waits for all of the thread's
-// outstanding loads, so no load may be in flight across a chunk hand-off.
-// The batch has the QK^T + softmax + first PV block of tile i to land.
+template <int L>
+__device__ __forceinline__ void load_phase_b(int q, ProdRegs<L>& R) {
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    const RowSrc& r = R.rs[k];
+    R.fb[0][k] = ldg_or_zero(r.valid, r.rec + 256 + 16 * q);
+    if constexpr (L == DSV4B_LAYOUT_V32) {
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
+    } else if (q < 4) {  // MODEL1 pair 3: fp8 columns 384..447 ...
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
+    } else {             // ... and the 64 bf16 RoPE columns
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
+      R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
+    }
+  }
+}
+
+// Folds registers into one word stored to shared memory: pins the loads
+// (and their completion) to this point, so the code generator cannot sink
+// them into the chunk loop where the latency would be exposed per chunk.
+template <int L>
+__device__ __forceinline__ void land_phase_a(const ProdRegs<L>& R, const int (&idx)[kRowsPerThread],
+                                             Misc& M) {
+  uint32_t x = 0;
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    x ^= R.fa[0][k].x ^ R.fa[0][k].y ^ R.fa[0][k].z ^ R.fa[0][k].w;
+    x ^= R.fa[1][k].x ^ R.fa[1][k].y ^ R.fa[1][k].z ^ R.fa[1][k].w;
+    x ^= R.sc[k].x ^ R.sc[k].y ^ R.sc[k].z ^ R.sc[k].w ^ (uint32_t)idx[k];
+  }
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(&M.sink_word)), "r"(x) : "memory");
+}
+
+// Scale of the 16 columns lane q holds in chunk pair m.
+template <int L>
+__device__ __forceinline__ float pair_scale(const uint4& sc, int m, int q) {
+  if constexpr (L == DSV4B_LAYOUT_V32) {
+    return __uint_as_float(m == 0 ? sc.x : m == 1 ? sc.y : m == 2 ? sc.z : sc.w);
+  } else {
+    const int byte = 2 * m + (q >> 2);  // 64-column UE8M0 tiles
+    const uint32_t w = byte < 4 ? sc.x : sc.y;
+    return ue8m0_to_f32((w >> (8 * (byte & 3))) & 0xFFu);
+  }
+}
+
+// Dequantises lane q's 16 e4m3 of chunk pair m of one row into its two
+// 16-byte units of chunk slot 2m + q/4.
+__device__ __forceinline__ void store_pair_fp8(uint32_t slot_s, int m, int row, int q, uint4 v,
+                                               float s) {
+  uint4 lo, hi;
+  dq16(v, s, lo, hi);
+  const uint32_t slot = slot_s + (2 * m + (q >> 2)) * kSlotBytes;
+  const int u = 2 * (q & 3);
+  sts_v4(slot + sw128_off(row, u), lo);
+  sts_v4(slot + sw128_off(row, u + 1), hi);
+}
+
 template <int L>
 __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                              uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
   using LT = LayoutT<L>;
   constexpr int NCH = LT::kChunks;
-  constexpr int NF = LT::kFp8Chunks;
   const int ptid = threadIdx.x;
-  const int row = ptid >> 1, half = ptid & 1;
+  const int w = ptid >> 5, lane = ptid & 31;
+  const int q = lane & 7;
+  const int row0 = 16 * w + (lane >> 3);  // row of pass k: row0 + 4k
 
   TileCursor cur = cursor_begin(p, sm);
   if (!cur.valid) return;
   TileCursor nxt = cursor_next(p, sm, cur);
 
-  ProducerRegs<L> R;
-  load_tile<L>(producer_row<L>(p, cur, producer_index(p, cur, row)), half, R);
-  int idx_next = nxt.valid ? producer_index(p, nxt, row) : -1;
+  ProdRegs<L> R;
+  int idx[kRowsPerThread];
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
+  rows_of<L>(p, cur, idx, R);
+  prefetch_rows_l2<L>(q, R);
+  load_phase_a<L>(q, R);
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nxt.valid ? producer_index(p, nxt, row0 + 4 * k) : -1;
+  land_phase_a<L>(R, idx, M);
 
   int tile_count = 0, seg_count = 0;
   volatile int* abort_flag = &M.abort;
@@ -230,32 +317,67 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
       if (ptid == 0) DSV4B_TR_ROLE(0, 5, seg_count);
       ++seg_count;
     }
-
     if (ptid == 0) DSV4B_TR_ROLE(0, 1, tile_count);
     const uint32_t wait_par = (tile_count - 1) & 1;
+
+    // pairs 0, 1 (phase A registers)
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      if (tile_count > 0 && !mbar_wait(&M.empty[empty_of<L>(c)], wait_par, abort_flag, err)) return;
-      if (ptid == 0) DSV4B_TR_ROLE(0, 3, c);
-      const uint32_t slot = slot_s + c * kSlotBytes;
-      if (c < 4) {
-        store_fp8_chunk(slot, row, half, R.a[2 * c], R.a[2 * c + 1], chunk_scale<L>(R.sc, c));
-      } else if (c < NF) {
-        store_fp8_chunk(slot, row, half, R.b[2 * (c - 4)], R.b[2 * (c - 4) + 1],
-                        chunk_scale<L>(R.sc, c));
-      } else {
+    for (int m = 0; m < 2; ++m) {
+      if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sts_v4(slot + sw128_off(row, 4 * half + i), R.b[2 * (NF - 4) + i]);
+      for (int k = 0; k < kRowsPerThread; ++k)
+        store_pair_fp8(slot_s, m, row0 + 4 * k, q, R.fa[m][k], pair_scale<L>(R.sc[k], m, q));
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[2 * m]);
+      mbar_arrive(&M.full[2 * m + 1]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+    }
+    load_phase_b<L>(q, R);
+    // pairs 2, 3 (phase B registers)
+#pragma unroll
+    for (int m = 2; m < 4; ++m) {
+      if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k) {
+        const int row = row0 + 4 * k;
+        if (L == DSV4B_LAYOUT_MODEL1 && m == 3 && q >= 4) {
+          const uint32_t slot = slot_s + 7 * kSlotBytes;  // MODEL1 RoPE chunk
+          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.fb[1][k]);
+          sts_v4(slot + sw128_off(row, 2 * (q - 4) + 1), R.rp[k]);
+        } else {
+          store_pair_fp8(slot_s, m, row, q, R.fb[m - 2][k], pair_scale<L>(R.sc[k], m, q));
+        }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&M.full[c]);
-      if (ptid == 0) DSV4B_TR_ROLE(0, 2, c);
+      mbar_arrive(&M.full[2 * m]);
+      mbar_arrive(&M.full[2 * m + 1]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+    }
+    if constexpr (LayoutT<L>::kPInRopeSlot) {
+      // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
+      // Its loads (L2 hits) overlap the wait for the previous PV.
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k)
+        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
+      if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
+      const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[NCH - 1]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
     }
 
-    // batch: data of the next tile, index of the one after
+    // batch: phase A of the next tile, indices of the one after
     const TileCursor nn = cursor_next(p, sm, nxt);
-    if (nxt.valid) load_tile<L>(producer_row<L>(p, nxt, idx_next), half, R);
-    idx_next = nn.valid ? producer_index(p, nn, row) : -1;
+    if (nxt.valid) {
+      rows_of<L>(p, nxt, idx, R);
+      prefetch_rows_l2<L>(q, R);
+      load_phase_a<L>(q, R);
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
+      land_phase_a<L>(R, idx, M);
+    }
     if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
     cur = nxt;
