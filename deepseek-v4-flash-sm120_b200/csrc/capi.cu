@@ -21,16 +21,15 @@ struct WsLayout {
   size_t lse_off, o_off, total;
 };
 
-// Workspace: [status word | lse_accum [splits][h_q] | o_accum [splits][head
-// groups][512 dims][64 heads]]; a query row split over k parts adds k - 1
-// splits, so b*s_q + parts bounds the split count.
+// Workspace: [status word | lse_accum [splits][h_q] | o_accum [splits][h_q]
+// [512]]; a query row split over k parts adds k - 1 splits, so b*s_q +
+// parts bounds the split count.
 inline WsLayout ws_layout(int b, int s_q, int h_q, int parts) {
   const size_t max_splits = (size_t)b * s_q + (size_t)parts;
-  const size_t groups = ((size_t)h_q + dsv4b::kHeadsPerCtaPublic - 1) / dsv4b::kHeadsPerCtaPublic;
   WsLayout w;
   w.lse_off = kStatusBytes;
   w.o_off = align_up(w.lse_off + max_splits * h_q * sizeof(float), 256);
-  w.total = align_up(w.o_off + max_splits * groups * dsv4b::kHeadsPerCtaPublic * 512 * sizeof(float), 256);
+  w.total = align_up(w.o_off + max_splits * (size_t)h_q * 512 * sizeof(float), 256);
   return w;
 }
 

@@ -12,8 +12,7 @@
 //
 // K3 merges splits: lse = log sum_i exp(lse_i), O = sum_i exp(lse_i - lse)
 // O_i, then the sink epilogue of tests/reference.py:124-129.  One CTA per
-// (query row, 64-head group, 64-dim block); rows with a single split were
-// written by K1 directly.
+// (query row, head); rows with a single split were written by K1 directly.
 #include <cuda_bf16.h>
 
 #include "dsv4b_internal.cuh"
@@ -139,76 +138,72 @@ __global__ void __launch_bounds__(kSchedThreads)
 }
 
 // ------------------------------------------------------------- combine
-// One CTA per (query row, 64-head group, 64-dim block), one thread per
-// output dim.  The decode kernel leaves split partials dims-major:
-// o_accum[split][group][dim][64 heads] (already divided by the split's own
-// row sum) and lse_accum[split][h_q].
-constexpr int kCombineThreads = 64;
-constexpr int kCombineDimBlocks = kDv / kCombineThreads;  // 8
+// One 128-thread CTA per (query row, head); thread t owns dims 4t..4t+3.
+// The decode kernel leaves split partials o_accum[split][h_q][512] (already
+// divided by the split's own row sum) and lse_accum[split][h_q].
+constexpr int kCombineThreads = kDv / 4;  // 128
 
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const dsv4b_decode_params p, const int32_t* __restrict__ num_splits,
                    const float* __restrict__ lse_accum, const float* __restrict__ o_accum) {
-  const int r = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
-  const int d = blockIdx.z * kCombineThreads + t;
+  const int r = blockIdx.x, head = blockIdx.y, t = threadIdx.x;
   const int s0 = __ldg(num_splits + r), s1 = __ldg(num_splits + r + 1);
   const int n = s1 - s0;
   if (n <= 1) return;  // written by the decode kernel
-  const int n_groups = gridDim.y;
-  __shared__ float s_lse[kHeadsPerCta];
-  __shared__ float s_w[2][kHeadsPerCta];
-  __shared__ float s_scale[kHeadsPerCta];
+  const float* lse_col = lse_accum + (int64_t)s0 * p.h_q + head;
+  float mx = -INFINITY;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(lse_col + (int64_t)i * p.h_q));
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += expf(__ldg(lse_col + (int64_t)i * p.h_q) - mx);
+  const float lse = mx + logf(sum);
+
+  const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)s0 * p.h_q + head) * kDv) + t;
+  const int64_t step = (int64_t)p.h_q * (kDv / 4);  // float4s between splits
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int i = 0;
+  for (; i + 4 <= n; i += 4) {
+    float4 v[4];
+    float w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = __ldg(src + (i + k) * step);
+      w[k] = expf(__ldg(lse_col + (int64_t)(i + k) * p.h_q) - lse);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc.x = fmaf(w[k], v[k].x, acc.x);
+      acc.y = fmaf(w[k], v[k].y, acc.y);
+      acc.z = fmaf(w[k], v[k].z, acc.z);
+      acc.w = fmaf(w[k], v[k].w, acc.w);
+    }
+  }
+  for (; i < n; ++i) {
+    const float4 v = __ldg(src + i * step);
+    const float wi = expf(__ldg(lse_col + (int64_t)i * p.h_q) - lse);
+    acc.x = fmaf(wi, v.x, acc.x);
+    acc.y = fmaf(wi, v.y, acc.y);
+    acc.z = fmaf(wi, v.z, acc.z);
+    acc.w = fmaf(wi, v.w, acc.w);
+  }
+  float scale = 1.0f, lse_out = lse;
+  if (p.attn_sink) {
+    const float sink = __ldg(p.attn_sink + head);
+    scale = 1.0f / (1.0f + expf(sink - lse));
+    if (p.lse_includes_sink) {
+      const float m = fmaxf(lse, sink);
+      lse_out = m + logf(expf(lse - m) + expf(sink - m));
+    }
+  }
   const int b = r / p.s_q, s = r - b * p.s_q;
-  {
-    const int head = g * kHeadsPerCta + t;
-    float lse = 0.0f, scale = 0.0f;
-    if (head < p.h_q) {
-      float mx = -INFINITY;
-      for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head));
-      float sum = 0.0f;
-      for (int i = 0; i < n; ++i) sum += expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - mx);
-      lse = mx + logf(sum);
-      float lse_out = lse;
-      scale = 1.0f;
-      if (p.attn_sink) {
-        const float sink = __ldg(p.attn_sink + head);
-        scale = 1.0f / (1.0f + expf(sink - lse));
-        if (p.lse_includes_sink) {
-          const float m = fmaxf(lse, sink);
-          lse_out = m + logf(expf(lse - m) + expf(sink - m));
-        }
-      }
-      if (blockIdx.z == 0) p.lse[((int64_t)b * p.h_q + head) * p.s_q + s] = lse_out;
-    }
-    s_lse[t] = lse;
-    s_scale[t] = scale;
-  }
-  __syncthreads();
-  float acc[kHeadsPerCta];
-#pragma unroll
-  for (int h = 0; h < kHeadsPerCta; ++h) acc[h] = 0.0f;
-  for (int i = 0; i < n; ++i) {
-    const int head = g * kHeadsPerCta + t;
-    s_w[i & 1][t] = head < p.h_q ? expf(__ldg(lse_accum + (int64_t)(s0 + i) * p.h_q + head) - s_lse[t]) : 0.0f;
-    __syncthreads();
-    const float4* src = reinterpret_cast<const float4*>(
-        o_accum + (((int64_t)(s0 + i) * n_groups + g) * kDv + d) * kHeadsPerCta);
-#pragma unroll
-    for (int h4 = 0; h4 < kHeadsPerCta / 4; ++h4) {
-      const float4 v = __ldg(src + h4);
-      acc[4 * h4 + 0] = fmaf(s_w[i & 1][4 * h4 + 0], v.x, acc[4 * h4 + 0]);
-      acc[4 * h4 + 1] = fmaf(s_w[i & 1][4 * h4 + 1], v.y, acc[4 * h4 + 1]);
-      acc[4 * h4 + 2] = fmaf(s_w[i & 1][4 * h4 + 2], v.z, acc[4 * h4 + 2]);
-      acc[4 * h4 + 3] = fmaf(s_w[i & 1][4 * h4 + 3], v.w, acc[4 * h4 + 3]);
-    }
-  }
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.stride_o_b +
-                       (int64_t)s * p.stride_o_s + d;
-#pragma unroll
-  for (int h = 0; h < kHeadsPerCta; ++h) {
-    const int head = g * kHeadsPerCta + h;
-    if (head < p.h_q) out[(int64_t)head * p.stride_o_h] = __float2bfloat16_rn(acc[h] * s_scale[h]);
-  }
+                       (int64_t)s * p.stride_o_s + (int64_t)head * p.stride_o_h + 4 * t;
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * scale, acc.y * scale);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * scale, acc.w * scale);
+  uint2 o;
+  o.x = *reinterpret_cast<const uint32_t*>(&lo);
+  o.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(out) = o;
+  if (t == 0) p.lse[((int64_t)b * p.h_q + head) * p.s_q + s] = lse_out;
 }
 
 // ------------------------------------------------------------- debug gather
@@ -264,7 +259,7 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
 
 cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
                            const float* lse_accum, const float* o_accum, cudaStream_t stream) {
-  const dim3 grid(p.b * p.s_q, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta, kCombineDimBlocks);
+  const dim3 grid(p.b * p.s_q, p.h_q);
   combine_kernel<<<grid, kCombineThreads, 0, stream>>>(p, num_splits, lse_accum, o_accum);
   return cudaGetLastError();
 }

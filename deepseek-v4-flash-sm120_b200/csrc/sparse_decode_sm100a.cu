@@ -455,7 +455,7 @@ __device__ __forceinline__ void apply_sink(float sink, int lse_includes_sink, fl
 
 // Epilogue of one (query row, split): row sums, LSE (+ sink for a row
 // finished in this CTA), then either the bf16 output (whole row here) or
-// the fp32 split partial, dims-major [split][group][dim][64 heads].
+// the fp32 split partial [split][h_q][512 dims].
 __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm,
                                          int g, const TileCursor& cur, float m_run,
                                          const int32_t* num_splits, float* lse_accum, float* o_accum,
@@ -523,23 +523,27 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
       named_bar_sync(1, kSoftmaxThreads);
     }
   } else {
-    const int n_groups = (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta;
+    // fp32 partial [split][h_q][512] through the same staging tile (16 heads x
+    // 128 dims per round): each row goes out as full 128-byte segments.
+    float* stage = reinterpret_cast<float*>(&M.stage[0][0]);  // [16][128] fp32
+    const int r = st >> 3, part = st & 7;
 #pragma unroll 1
-    for (int m = 0; m < 4; ++m) {
-      float4* dst = reinterpret_cast<float4*>(
-          o_accum + (((int64_t)split * n_groups + g) * kDv + 128 * m + st) * kHeadsPerCta);
+    for (int mg = 0; mg < 16; ++mg) {  // 4 M-blocks x 4 groups of 16 heads
+      const int m = mg >> 2, hg = mg & 3;
+      float ov[16];
+      tmem_ld16(tl + kColO + 64 * m + 16 * hg, ov);
+      tc_wait_ld();
 #pragma unroll
-      for (int c16 = 0; c16 < 4; ++c16) {
-        float ov[16];
-        tmem_ld16(tl + kColO + 64 * m + 16 * c16, ov);
-        tc_wait_ld();
+      for (int j = 0; j < 16; ++j) stage[j * 128 + st] = ov[j] * M.scale_o[16 * hg + j];
+      named_bar_sync(1, kSoftmaxThreads);
+      const int head = g * kHeadsPerCta + 16 * hg + r;
+      if (head < p.h_q) {
+        float4* dst = reinterpret_cast<float4*>(o_accum + ((int64_t)split * p.h_q + head) * kDv + 128 * m);
+        const float4* src = reinterpret_cast<const float4*>(stage + r * 128);
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 sc = *reinterpret_cast<const float4*>(&M.scale_o[16 * c16 + 4 * j4]);
-          dst[4 * c16 + j4] = make_float4(ov[4 * j4] * sc.x, ov[4 * j4 + 1] * sc.y,
-                                          ov[4 * j4 + 2] * sc.z, ov[4 * j4 + 3] * sc.w);
-        }
+        for (int k = 0; k < 4; ++k) dst[8 * k + part] = src[8 * k + part];
       }
+      named_bar_sync(1, kSoftmaxThreads);
     }
   }
 }
