@@ -114,6 +114,30 @@ int check_workspace(const dsv4b_decode_params* p, int parts, void* ws, size_t ws
   return DSV4B_OK;
 }
 
+// Built-in scratch for dsv4b_sparse_decode_noalloc: every GPU that loads the
+// library holds DSV4B_NOALLOC_SCRATCH_BYTES of it until process exit.  In
+// host code the name is only a host-side stand-in; the device address comes
+// from cudaGetSymbolAddress (per device, with that device current).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DSV4B_NOALLOC_SCRATCH_BYTES];
+
+void* g_noalloc_ptr[64];  // device address of g_noalloc_scratch, per device
+
+// Device address of this device's scratch; looked up once per device (the
+// first call on a device), never allocates.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSV4B_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) return cuda_rc(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSV4B_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -129,6 +153,8 @@ const char* dsv4b_status_string(int status) {
     case DSV4B_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case DSV4B_ERR_ARCH: return "device is not an sm_100 (B200-class) GPU";
     case DSV4B_ERR_KERNEL_TIMEOUT: return "a kernel wait hit its time limit";
+    case DSV4B_ERR_SCRATCH_LIMIT:
+      return "request exceeds the fixed 32 MiB no-allocation scratch (use dsv4b_sparse_decode)";
     default: return "unknown status";
   }
 }
@@ -218,6 +244,31 @@ int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks, int page_bl
   return cuda_rc(dsv4b::launch_gather_dequant(layout, kv, num_blocks, page_block_size, stride_kv_block,
                                               stride_kv_row, indices, n, out_bf16,
                                               static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
+                                const int32_t* num_splits, int num_sm_parts, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (!sched_meta || !num_splits || num_sm_parts <= 0 || num_sm_parts > 65535)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  const WsLayout w = ws_layout(p->b, p->s_q, p->h_q, num_sm_parts);
+  if (w.total > (size_t)DSV4B_NOALLOC_SCRATCH_BYTES) return DSV4B_ERR_SCRATCH_LIMIT;
+  if ((rc = current_arch_ok())) return rc;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(scratch);
+  // The status word must start at zero; the partials are fully written
+  // before they are read, so nothing else needs clearing.
+  if ((rc = cuda_rc(cudaMemsetAsync(ws, 0, kStatusBytes, s)))) return rc;
+  if ((rc = cuda_rc(dsv4b::launch_sparse_decode(*p, sched_meta, num_splits, num_sm_parts,
+                                                reinterpret_cast<float*>(ws + w.lse_off),
+                                                reinterpret_cast<float*>(ws + w.o_off),
+                                                reinterpret_cast<int*>(ws), s))))
+    return rc;
+  return cuda_rc(dsv4b::launch_combine(*p, num_splits, reinterpret_cast<const float*>(ws + w.lse_off),
+                                       reinterpret_cast<const float*>(ws + w.o_off), s));
 }
 
 int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes, int* flags, void* stream) {

@@ -22,6 +22,7 @@ STATUS = {
     -4: "DSV4B_ERR_WORKSPACE",
     -5: "DSV4B_ERR_ARCH",
     -6: "DSV4B_ERR_KERNEL_TIMEOUT",
+    -7: "DSV4B_ERR_SCRATCH_LIMIT",
 }
 
 # Every symbol include/dsv4b.h declares (checked by tests/test_abi.py).
@@ -29,8 +30,10 @@ EXPORTED = (
     "dsv4b_version", "dsv4b_status_string", "dsv4b_check_device",
     "dsv4b_num_sm_parts", "dsv4b_workspace_bytes", "dsv4b_get_mla_metadata",
     "dsv4b_sparse_decode", "dsv4b_combine", "dsv4b_sparse_decode_partial",
-    "dsv4b_gather_dequant", "dsv4b_read_kernel_status",
+    "dsv4b_gather_dequant", "dsv4b_read_kernel_status", "dsv4b_sparse_decode_noalloc",
 )
+
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -85,6 +88,7 @@ def _load():
     lib.dsv4b_combine.argtypes = [P, _vp, ctypes.c_int, _vp, ctypes.c_size_t, _vp]
     lib.dsv4b_gather_dequant.argtypes = [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int,
                                          _i64, _i64, _vp, ctypes.c_int, _vp, _vp]
+    lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]
     lib.dsv4b_read_kernel_status.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int), _vp]
     return lib
 

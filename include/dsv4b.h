@@ -35,7 +35,9 @@ typedef enum dsv4b_status {
   DSV4B_ERR_CUDA = -3,             /* a CUDA runtime call failed */
   DSV4B_ERR_WORKSPACE = -4,        /* workspace too small */
   DSV4B_ERR_ARCH = -5,             /* device is not sm_100 */
-  DSV4B_ERR_KERNEL_TIMEOUT = -6    /* a kernel wait hit its time limit */
+  DSV4B_ERR_KERNEL_TIMEOUT = -6,   /* a kernel wait hit its time limit */
+  DSV4B_ERR_SCRATCH_LIMIT = -7     /* request needs more than the fixed
+                                      scratch of dsv4b_sparse_decode_noalloc */
 } dsv4b_status;
 
 /* KV-cache byte layouts (csrc/common/params.h:12-15, ModelType). */
@@ -170,6 +172,32 @@ DSV4B_API int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks,
  * *flags (0 = no error).  Synchronises `stream`. */
 DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
                              int* flags, void* stream);
+
+/* Size of the library's built-in device scratch used by
+ * dsv4b_sparse_decode_noalloc (32 MiB per GPU that loads the library). */
+#define DSV4B_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* Sparse decode forward that allocates nothing.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory at
+ * call time -- e.g. a serving engine that has already handed all free HBM
+ * to its KV-cache pool, or a C / FFI caller that has no access to a caching
+ * allocator and must not call cudaMalloc in the middle of a decode step
+ * (cudaMalloc can synchronise the device).  Same inputs, outputs and
+ * results as dsv4b_sparse_decode, but the split-KV partials and the kernel
+ * status word live in a fixed DSV4B_NOALLOC_SCRATCH_BYTES array inside the
+ * library instead of a caller workspace; requests whose workspace
+ * (dsv4b_workspace_bytes) would exceed it return DSV4B_ERR_SCRATCH_LIMIT
+ * before launching anything.  The first call on a device looks up that
+ * device's scratch address (a one-time runtime query, no allocation), so
+ * make the first call on each device before any stream capture.  All calls
+ * on a device share the one scratch array and it keeps the last call's
+ * contents (the status word is cleared at the start of every call): calls
+ * that overlap on the GPU -- different streams without ordering between
+ * them -- race on it and must not be issued. */
+DSV4B_API int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p,
+                                          const dsv4b_sched_meta* sched_meta,
+                                          const int32_t* num_splits, int num_sm_parts,
+                                          void* stream);
 
 #ifdef __cplusplus
 }
