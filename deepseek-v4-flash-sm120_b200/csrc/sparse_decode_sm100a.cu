@@ -86,6 +86,10 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Misc {
+  // Epilogue transpose tile (8 KB).  Between epilogues it holds bf16 ones:
+  // the A operand of the row-sum UMMA (ones[64 x 128 tok] . P^T), so it
+  // sits at offset 0, 1024-byte aligned like every SW128 operand.
+  __nv_bfloat16 stage[32][128];
   uint64_t full[9];
   uint64_t empty[5];
   uint64_t s_full, p_full, q_full, q_empty, o_full;
@@ -97,12 +101,11 @@ struct Misc {
   alignas(16) float m_use[64];    // read as float4
   alignas(16) float alpha[64];
   alignas(16) float scale_o[64];
-  alignas(16) __nv_bfloat16 stage[32][128];  // epilogue transpose tile (8 KB)
 };
 static_assert(offsetof(Misc, red) % 16 == 0 && offsetof(Misc, m_use) % 16 == 0 &&
-                  offsetof(Misc, alpha) % 16 == 0 && offsetof(Misc, scale_o) % 16 == 0 &&
-                  offsetof(Misc, stage) % 16 == 0,
+                  offsetof(Misc, alpha) % 16 == 0 && offsetof(Misc, scale_o) % 16 == 0,
               "Misc float arrays must be 16-byte aligned (vector shared-memory loads)");
+static_assert(offsetof(Misc, stage) == 0, "stage must start Misc (SW128 operand)");
 static_assert(sizeof(Misc) % 16 == 0, "Misc size");
 
 template <int L>
@@ -117,14 +120,11 @@ struct SmemPlan {
   static constexpr int kBytes = kMiscOff + (int)sizeof(Misc) + 1024;  // + alignment slack
 };
 
+static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kMiscOff % 1024 == 0 &&
+                  SmemPlan<DSV4B_LAYOUT_MODEL1>::kMiscOff % 1024 == 0,
+              "Misc must be 1024-byte aligned");
 static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kBytes <= 232448, "V32 smem plan too large");
 static_assert(SmemPlan<DSV4B_LAYOUT_MODEL1>::kBytes <= 232448, "MODEL1 smem plan too large");
-
-__device__ __forceinline__ float warp_sum_f32(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 o = __floats2bfloat162_rn(a, b);
@@ -393,6 +393,8 @@ __device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm
   constexpr int NCH = LayoutT<L>::kChunks;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 64, false, false);
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 64, true, true);
+  constexpr uint32_t idesc_sum = idesc_bf16_f32(64, 64, false, true);
+  const uint32_t ones_s = smem_u32(&M.stage[0][0]);
   volatile int* abort_flag = &M.abort;
 
   TileCursor cur = cursor_begin(p, sm);
@@ -434,6 +436,13 @@ __device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm
       }
       umma_commit(&M.empty[m]);
     }
+    // Row sums on the tensor core: L[64 x heads] += ones[64 x 128 tok] .
+    // P^T, so every row of L (TMEM lane 0 included) holds sum_tok P for
+    // each head, summed from the same bf16 P that enters O.
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      umma_bf16_ss(tmem + kColL, sdesc_sw128(ones_s, 16, 1024), sdesc_sw128(p_s + kk * 2048, 8192, 1024),
+                   idesc_sum, !(seg_first && kk == 0));
     if (LayoutT<L>::kPInRopeSlot) umma_commit(&M.empty[4]);
     DSV4B_TR_ROLE(1, 13, tile_count);
     if (seg_last) umma_commit(&M.o_full);
@@ -462,22 +471,25 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
                                          uint32_t tl, Misc& M) {
   const int st = threadIdx.x - kProducerThreads;
   const int q = st >> 5, lane = st & 31;
+  // Row sums: the row-sum UMMA left sum_tok P of head j in column kColL + j
+  // of every row; warp 0 reads TMEM lane 0.
+  if (q == 0) {
 #pragma unroll
-  for (int c16 = 0; c16 < 4; ++c16) {
-    float lv[16];
-    tmem_ld16(tl + kColL + 16 * c16, lv);
-    tc_wait_ld();
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float lv[16];
+      tmem_ld16(tl + kColL + 16 * c16, lv);
+      tc_wait_ld();
+      if (lane == 0) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float v = warp_sum_f32(lv[j]);
-      if (lane == 0) M.red[q][16 * c16 + j] = v;
+        for (int j = 0; j < 16; ++j) M.red[0][16 * c16 + j] = lv[j];
+      }
     }
   }
   named_bar_sync(1, kSoftmaxThreads);
   const bool final_out = (cur.t_lo == 0 && cur.t_hi == cur.ri.nt);
   const int split = (cur.req == sm.begin_req_idx) ? sm.begin_split_idx : __ldg(num_splits + cur.req);
   if (st < 64) {
-    const float l = (M.red[0][st] + M.red[1][st]) + (M.red[2][st] + M.red[3][st]);
+    const float l = M.red[0][st];
     const int head = g * kHeadsPerCta + st;
     float lse = (m_run + log2f(l)) * kLn2;
     float scale = 1.0f / l;
@@ -548,12 +560,105 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
   }
 }
 
+// Writes bf16 ones over the staging tile (the row-sum UMMA's A operand)
+// and makes them visible to the tensor core.
+__device__ __forceinline__ void fill_ones(Misc& M, int st) {
+  uint4* dst = reinterpret_cast<uint4*>(&M.stage[0][0]);
+  const uint4 one = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+#pragma unroll
+  for (int i = st; i < (int)(sizeof(M.stage) / 16); i += kSoftmaxThreads) dst[i] = one;
+  fence_proxy_async_smem();
+}
+
+// Per-head stabiliser update: column max of the tile via redux.sync and a
+// 4-warp exchange, m_use / alpha for every head, and, when some head's max
+// rose by more than 2^8 after the row's first tile, the rescale of that
+// head's O and row-sum columns in TMEM.
+__device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, bool seg_first,
+                                                 float& m_run, Misc& M) {
+  const int st = threadIdx.x - kProducerThreads;
+  const int q = st >> 5, lane = st & 31;
+#pragma unroll
+  for (int c16 = 0; c16 < 4; ++c16) {
+    float sv[16];
+    tmem_ld16(tl + kColS + 16 * c16, sv);
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float mx = warp_max_f32(row_scale != 0.0f ? sv[j] * row_scale : -INFINITY);
+      if (lane == 0) M.red[q][16 * c16 + j] = mx;
+    }
+  }
+  named_bar_sync(1, kSoftmaxThreads);
+  bool resc = false;
+  if (st < 64) {
+    const float mt = fmaxf(fmaxf(M.red[0][st], M.red[1][st]), fmaxf(M.red[2][st], M.red[3][st]));
+    const float m_old = m_run;
+    float m_new = m_old, alpha = 1.0f;
+    if (m_old == -INFINITY) {
+      m_new = mt;
+    } else if (mt > m_old + kRescaleThreshold) {
+      m_new = mt;
+      alpha = fast_exp2(m_old - m_new);
+      resc = true;
+    }
+    m_run = m_new;
+    M.m_use[st] = (m_new == -INFINITY) ? 0.0f : m_new;
+    M.alpha[st] = alpha;
+  }
+  const bool any_resc = named_bar_or(1, kSoftmaxThreads, resc);
+  if (any_resc && !seg_first) {
+    // 16 O column groups (4 M-blocks x 64 heads) + 4 row-sum groups.
+#pragma unroll 1
+    for (int cc = 0; cc < 20; ++cc) {
+      const uint32_t col = cc < 16 ? kColO + 64 * (cc >> 2) + 16 * (cc & 3) : kColL + 16 * (cc - 16);
+      float ov[16];
+      tmem_ld16(tl + col, ov);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ov[j] *= M.alpha[16 * (cc & 3) + j];
+      tmem_st16(tl + col, ov);
+    }
+  }
+}
+
+// P = 2^(s * scale - m_use) rounded to bf16, stored as P^T row st in
+// shared memory.  Returns whether any of this row's logits exceeds its
+// head's stabiliser by more than 2^8 (the P just written is then redone).
+__device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uint32_t p_s,
+                                               const Misc& M) {
+  const int st = threadIdx.x - kProducerThreads;
+  bool exceed = false;
+#pragma unroll
+  for (int c16 = 0; c16 < 4; ++c16) {
+    float sv[16];
+    tmem_ld16(tl + kColS + 16 * c16, sv);
+    tc_wait_ld();
+    uint32_t pk[8];
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
+      const float x0 = fmaf(sv[4 * j4 + 0], row_scale, -mu.x);
+      const float x1 = fmaf(sv[4 * j4 + 1], row_scale, -mu.y);
+      const float x2 = fmaf(sv[4 * j4 + 2], row_scale, -mu.z);
+      const float x3 = fmaf(sv[4 * j4 + 3], row_scale, -mu.w);
+      exceed |= (fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)) > kRescaleThreshold);
+      const bool live = row_scale != 0.0f;
+      pk[2 * j4] = pack_bf16(live ? fast_exp2(x0) : 0.0f, live ? fast_exp2(x1) : 0.0f);
+      pk[2 * j4 + 1] = pack_bf16(live ? fast_exp2(x2) : 0.0f, live ? fast_exp2(x3) : 0.0f);
+    }
+    sts_v4(p_s + sw128_off(st, 2 * c16), make_uint4(pk[0], pk[1], pk[2], pk[3]));
+    sts_v4(p_s + sw128_off(st, 2 * c16 + 1), make_uint4(pk[4], pk[5], pk[6], pk[7]));
+  }
+  return exceed && row_scale != 0.0f;
+}
+
 template <int L>
 __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                             const int32_t* num_splits, float* lse_accum, float* o_accum,
                             uint32_t p_s, uint32_t tmem, Misc& M, int* err) {
   const int st = threadIdx.x - kProducerThreads;  // 0..127 = token row = TMEM lane
-  const int q = st >> 5, lane = st & 31;
+  const int q = st >> 5;
   const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
   const float scale_log2 = p.sm_scale * kLog2e;
   volatile int* abort_flag = &M.abort;
@@ -571,112 +676,18 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     if (st == 0) DSV4B_TR_ROLE(2, 20, tile_count);
     tc_fence_after();
 
-    // Phase 1.  After a row's first tile the stabiliser m_use is kept unless
-    // some logit exceeds it by more than 2^8: one vote instead of a
-    // cross-warp max exchange per tile.
-    // (tcgen05.ld / wait::ld are .sync.aligned: every lane must execute
-    // them, padding rows included, so only the compare is masked.)
-    bool need = seg_first;
-    if (!seg_first) {
-#pragma unroll
-      for (int c16 = 0; c16 < 4; ++c16) {
-        float sv[16];
-        tmem_ld16(tl + kColS + 16 * c16, sv);
-        tc_wait_ld();
-#pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
-          need |= (row_scale != 0.0f) & ((sv[4 * j4] * row_scale > mu.x + kRescaleThreshold) |
-                                         (sv[4 * j4 + 1] * row_scale > mu.y + kRescaleThreshold) |
-                                         (sv[4 * j4 + 2] * row_scale > mu.z + kRescaleThreshold) |
-                                         (sv[4 * j4 + 3] * row_scale > mu.w + kRescaleThreshold));
-        }
-      }
-    }
-    bool any_resc = false;
-    if (named_bar_or(1, kSoftmaxThreads, need)) {
-      // Column (per-head) max of the tile via redux.sync + a 4-warp exchange.
-#pragma unroll
-      for (int c16 = 0; c16 < 4; ++c16) {
-        float sv[16];
-        tmem_ld16(tl + kColS + 16 * c16, sv);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float mx = warp_max_f32(row_scale != 0.0f ? sv[j] * row_scale : -INFINITY);
-          if (lane == 0) M.red[q][16 * c16 + j] = mx;
-        }
-      }
-      named_bar_sync(1, kSoftmaxThreads);
-      bool resc = false;
-      if (st < 64) {
-        const float mt = fmaxf(fmaxf(M.red[0][st], M.red[1][st]), fmaxf(M.red[2][st], M.red[3][st]));
-        const float m_old = m_run;
-        float m_new = m_old, alpha = 1.0f;
-        if (m_old == -INFINITY) {
-          m_new = mt;
-        } else if (mt > m_old + kRescaleThreshold) {
-          m_new = mt;
-          alpha = fast_exp2(m_old - m_new);
-          resc = true;
-        }
-        m_run = m_new;
-        M.m_use[st] = (m_new == -INFINITY) ? 0.0f : m_new;
-        M.alpha[st] = alpha;
-      }
-      any_resc = named_bar_or(1, kSoftmaxThreads, resc);
-    }
-    if (st == 0) DSV4B_TR_ROLE(2, 21, any_resc);
-
-    // Phase 2.  P = 2^(s - m) rounded to bf16 -> P^T row st in shared
-    // memory; per-lane partial row sums (TMEM columns kColL..) += same P.
-#pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float sv[16];
-      tmem_ld16(tl + kColS + 16 * c16, sv);
-      float lv[16];
-      if (!seg_first) tmem_ld16(tl + kColL + 16 * c16, lv);
-      tc_wait_ld();
-      uint32_t pk[8];
-#pragma unroll
-      for (int j4 = 0; j4 < 4; ++j4) {
-        const float4 mu = *reinterpret_cast<const float4*>(&M.m_use[16 * c16 + 4 * j4]);
-        const float e0 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 0], row_scale, -mu.x)) : 0.0f;
-        const float e1 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 1], row_scale, -mu.y)) : 0.0f;
-        const float e2 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 2], row_scale, -mu.z)) : 0.0f;
-        const float e3 = row_scale != 0.0f ? fast_exp2(fmaf(sv[4 * j4 + 3], row_scale, -mu.w)) : 0.0f;
-        pk[2 * j4] = pack_bf16(e0, e1);
-        pk[2 * j4 + 1] = pack_bf16(e2, e3);
-      }
-      sts_v4(p_s + sw128_off(st, 2 * c16), make_uint4(pk[0], pk[1], pk[2], pk[3]));
-      sts_v4(p_s + sw128_off(st, 2 * c16 + 1), make_uint4(pk[4], pk[5], pk[6], pk[7]));
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float p0 = __uint_as_float(pk[j] << 16), p1 = __uint_as_float(pk[j] & 0xFFFF0000u);
-        if (seg_first) {
-          lv[2 * j] = p0;
-          lv[2 * j + 1] = p1;
-        } else {
-          const float a0 = any_resc ? M.alpha[16 * c16 + 2 * j] : 1.0f;
-          const float a1 = any_resc ? M.alpha[16 * c16 + 2 * j + 1] : 1.0f;
-          lv[2 * j] = fmaf(lv[2 * j], a0, p0);
-          lv[2 * j + 1] = fmaf(lv[2 * j + 1], a1, p1);
-        }
-      }
-      tmem_st16(tl + kColL + 16 * c16, lv);
-    }
-    // Lazy O rescale (only when some head's max rose by more than 2^8).
-    if (any_resc && !seg_first) {
-#pragma unroll 1
-      for (int cc = 0; cc < 16; ++cc) {  // 4 M-blocks x 4 column groups
-        const uint32_t col = kColO + 64 * (cc >> 2) + 16 * (cc & 3);
-        float ov[16];
-        tmem_ld16(tl + col, ov);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) ov[j] *= M.alpha[16 * (cc & 3) + j];
-        tmem_st16(tl + col, ov);
-      }
+    // A row's first tile sets the stabilisers.  After that the kept
+    // stabilisers are used directly; only when some logit exceeds its
+    // head's by more than 2^8 (a block-wide vote) are they raised, O and
+    // the row sums rescaled and P recomputed.
+    // (tcgen05.ld / wait::ld are .sync.aligned: every lane executes them,
+    // padding rows included.)
+    if (seg_first) {
+      softmax_max_path(tl, row_scale, true, m_run, M);
+      softmax_p_pass(tl, row_scale, p_s, M);
+    } else if (named_bar_or(1, kSoftmaxThreads, softmax_p_pass(tl, row_scale, p_s, M))) {
+      softmax_max_path(tl, row_scale, false, m_run, M);
+      softmax_p_pass(tl, row_scale, p_s, M);
     }
     tc_wait_st();
     fence_proxy_async_smem();
@@ -689,6 +700,8 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
       if (st == 0) DSV4B_TR_ROLE(2, 24, seg_count);
       tc_fence_after();
       epilogue(p, sm, g, cur, m_run, num_splits, lse_accum, o_accum, tl, M);
+      named_bar_sync(1, kSoftmaxThreads);  // staging tile reads done
+      fill_ones(M, st);
       tc_fence_before();
       if (st == 0) DSV4B_TR_ROLE(2, 25, seg_count);
       ++seg_count;
@@ -733,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
     fence_mbarrier_init();
   }
+  if (warp >= kProducerWarps && warp < kMmaWarp) fill_ones(M, threadIdx.x - kProducerThreads);
   if (warp == kMmaWarp) {
     tmem_alloc(&M.tmem_base, kTmemCols);
     tmem_relinquish();
