@@ -4,7 +4,11 @@
 // K2 replaces the reference's placeholder scheduler tensors
 // (csrc/api/sparse_decode.cpp:147-158, num_sm_parts = 1) with a real
 // plan: every query row r = b*s_q + s owns ceil(len/128) main tiles plus
-// ceil(extra_len/128) extra tiles; the concatenated tile list is cut into
+// ceil(extra_len/128) extra tiles.  With no more rows than parts the plan
+// is row-aligned: t* is the smallest per-part tile cap with
+// sum_r ceil(tiles_r / t*) <= parts and row r is shared evenly by
+// ceil(tiles_r / t*) parts, so no CTA switches rows (one Q load and one
+// epilogue each).  Otherwise the concatenated tile list is cut into
 // min(num_sm_parts, total tiles) contiguous, equal (+-1 tile) ranges, one
 // per decode CTA column.  A row cut by a range boundary becomes several
 // splits whose partial (O, LSE) the combine kernel merges.  Everything
@@ -61,10 +65,13 @@ __device__ __forceinline__ int part_of_tile(long long t, long long T, long long 
 __global__ void __launch_bounds__(kSchedThreads)
     sched_meta_kernel(const dsv4b_decode_params p, int num_sm_parts, dsv4b_sched_meta* sched,
                       int32_t* num_splits) {
-  extern __shared__ int sh[];
+  // scratch first: its base stays 16-byte aligned whatever R is, so the
+  // 32-entry reductions over it may be read as vectors.
+  extern __shared__ __align__(16) int sh[];
   const int R = p.b * p.s_q;
-  int* tile_off = sh;          // [R + 1]
-  int* scratch = sh + R + 1;   // [32]
+  int* scratch = sh;                // [32]
+  int* tile_off = sh + 32;          // [R + 1]
+  int* part_off = sh + 32 + R + 1;  // [R + 1] (row-aligned plan)
 
   // 1. tiles per query row -> exclusive prefix
   int carry = 0;
@@ -80,6 +87,73 @@ __global__ void __launch_bounds__(kSchedThreads)
   __syncthreads();
   const long long T = tile_off[R];
   const int P_eff = (int)min((long long)num_sm_parts, T);
+
+  if (R <= num_sm_parts) {
+    // Row-aligned plan.  t* by bisection over [1, max_r tiles_r] (the
+    // upper end always fits since R <= parts); every step is uniform
+    // across the block.
+    int max_t = 0;
+    for (int r = threadIdx.x; r < R; r += kSchedThreads) max_t = max(max_t, tile_off[r + 1] - tile_off[r]);
+    for (int o = 16; o > 0; o >>= 1) max_t = max(max_t, __shfl_xor_sync(0xffffffffu, max_t, o));
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = max_t;
+    __syncthreads();
+    int hi = 0;
+    for (int w = 0; w < kSchedThreads / 32; ++w) hi = max(hi, scratch[w]);
+    int lo = 1;
+    __syncthreads();
+    while (lo < hi) {
+      const int mid = (lo + hi) / 2;
+      int tot_parts = 0;
+      for (int base = 0; base < R; base += kSchedThreads) {
+        const int r = base + threadIdx.x;
+        const int n = r < R ? (tile_off[r + 1] - tile_off[r] + mid - 1) / mid : 0;
+        int tot;
+        block_exclusive_scan(n, scratch, &tot);
+        tot_parts += tot;
+      }
+      if (tot_parts <= num_sm_parts) hi = mid; else lo = mid + 1;
+    }
+    const int tcap = lo;
+    carry = 0;
+    for (int base = 0; base < R; base += kSchedThreads) {
+      const int r = base + threadIdx.x;
+      const int k = r < R ? (tile_off[r + 1] - tile_off[r] + tcap - 1) / tcap : 0;
+      int tot;
+      const int ex = block_exclusive_scan(k, scratch, &tot);
+      if (r < R) part_off[r] = num_splits[r] = carry + ex;
+      carry += tot;
+    }
+    if (threadIdx.x == 0) part_off[R] = num_splits[R] = carry;
+    __syncthreads();
+    for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+      dsv4b_sched_meta m;
+      if (part >= part_off[R]) {
+        m.begin_req_idx = 0;
+        m.end_req_idx = -1;
+        m.begin_block_idx = m.end_block_idx = 0;
+        m.begin_split_idx = 0;
+        m.is_first_req_splitted = m.is_last_req_splitted = 0;
+        m.num_tiles = 0;
+      } else {
+        int a = 0, z = R - 1;  // the row r with part_off[r] <= part < part_off[r + 1]
+        while (a < z) {
+          const int mid = (a + z + 1) >> 1;
+          if (part_off[mid] <= part) a = mid; else z = mid - 1;
+        }
+        const int r = a, j = part - part_off[r], k = part_off[r + 1] - part_off[r];
+        const int n = tile_off[r + 1] - tile_off[r];
+        m.begin_req_idx = m.end_req_idx = r;
+        m.begin_block_idx = (int)((long long)j * n / k);
+        m.end_block_idx = (int)((long long)(j + 1) * n / k);
+        m.begin_split_idx = part_off[r] + j;
+        m.is_first_req_splitted = m.begin_block_idx > 0;
+        m.is_last_req_splitted = m.end_block_idx < n;
+        m.num_tiles = m.end_block_idx - m.begin_block_idx;
+      }
+      sched[part] = m;
+    }
+    return;
+  }
 
   // 2. splits per row -> exclusive prefix = num_splits
   carry = 0;
@@ -242,14 +316,14 @@ __global__ void gather_dequant_kernel(const uint8_t* kv, int num_blocks, int pag
 cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
                               dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream) {
   const int R = p.b * p.s_q;
-  const size_t smem = (size_t)(R + 1 + 32) * sizeof(int);
+  const size_t smem = (size_t)(32 + 2 * (R + 1)) * sizeof(int);
   static bool attr_done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     e = cudaFuncSetAttribute(sched_meta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)((kMaxSchedRows + 1 + 32) * sizeof(int)));
+                             (int)((32 + 2 * (kMaxSchedRows + 1)) * sizeof(int)));
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }

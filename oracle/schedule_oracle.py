@@ -7,9 +7,16 @@ num_sm_parts = 1); the record format is its DecodingSchedMeta
 (csrc/common/params.h:17-32).  Plan: query row r = b*s_q + s owns
 ceil(len_main/128) + ceil(len_extra/128) tiles, len_main =
 max(min(topk_length[b], topk), 1) (tests/reference.py:107-109),
-len_extra = clamp(extra_topk_length[b], 0, extra_topk); the concatenated
-tile list is cut into P = min(num_sm_parts, T) ranges
-[floor(p*T/P), floor((p+1)*T/P)).
+len_extra = clamp(extra_topk_length[b], 0, extra_topk).
+
+* R <= num_sm_parts (row-aligned): t* = the smallest per-part tile cap with
+  sum_r ceil(tiles_r / t*) <= num_sm_parts; row r gets k_r =
+  ceil(tiles_r / t*) consecutive parts and its part j covers tiles
+  [floor(j*n/k), floor((j+1)*n/k)).  No part spans two rows.
+* otherwise (contiguous): the concatenated tile list is cut into
+  P = min(num_sm_parts, T) ranges [floor(p*T/P), floor((p+1)*T/P)).
+
+Parts past the last planned one get the empty record [0, -1, 0...].
 """
 from __future__ import annotations
 
@@ -34,9 +41,37 @@ def row_tiles(b: int, s_q: int, topk: int, topk_length: Optional[Sequence[int]],
     return out
 
 
+EMPTY = [0, -1, 0, 0, 0, 0, 0, 0]
+
+
+def _plan_row_aligned(tiles: Sequence[int], num_sm_parts: int):
+    R = len(tiles)
+    lo, hi = 1, max(tiles)
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if sum(-(-n // mid) for n in tiles) <= num_sm_parts:
+            hi = mid
+        else:
+            lo = mid + 1
+    k = [-(-n // lo) for n in tiles]
+    ns = [0]
+    for kr in k:
+        ns.append(ns[-1] + kr)
+    recs = []
+    for r in range(R):
+        n = tiles[r]
+        for j in range(k[r]):
+            bb, eb = j * n // k[r], (j + 1) * n // k[r]
+            recs.append([r, r, bb, eb, ns[r] + j, int(bb > 0), int(eb < n), eb - bb])
+    recs += [list(EMPTY) for _ in range(num_sm_parts - len(recs))]
+    return recs, ns
+
+
 def plan(tiles: Sequence[int], num_sm_parts: int) -> Tuple[List[List[int]], List[int]]:
     """Returns (records [num_sm_parts][8], num_splits [R+1])."""
     R = len(tiles)
+    if R <= num_sm_parts:
+        return _plan_row_aligned(tiles, num_sm_parts)
     off = [0]
     for n in tiles:
         off.append(off[-1] + n)
@@ -64,7 +99,7 @@ def plan(tiles: Sequence[int], num_sm_parts: int) -> Tuple[List[List[int]], List
     recs = []
     for p in range(num_sm_parts):
         if p >= P:
-            recs.append([0, -1, 0, 0, 0, 0, 0, 0])
+            recs.append(list(EMPTY))
             continue
         t0, t1 = p * T // P, (p + 1) * T // P
         br, er = row_of(t0), row_of(t1 - 1)

@@ -167,6 +167,25 @@ def test_split_counts_agree(parts):
     assert ns.cpu().tolist() == want_ns
 
 
+@pytest.mark.parametrize("b,s_q,topk,parts", [(2, 1, 64, 148), (2, 1, 256, 74), (32, 1, 2048, 148),
+                                              (3, 1, 1000, 7), (5, 3, 900, 148), (200, 1, 512, 148),
+                                              (1, 1, 4096, 148)])
+def test_scheduler_records_match_oracle(b, s_q, topk, parts):
+    """The device scheduler's records equal the restated plan, in both the
+    row-aligned (rows <= parts) and the contiguous mode, including row
+    counts whose shared-memory tables start at odd offsets."""
+    from deepseek_v4_kernel import ops
+    spec = _kc().BatchSpec(b=b, s_q=s_q, h_q=64, topk=topk, ctx=8192, page_block=64, seed=3)
+    bt = _kc().make_batch(spec)
+    out = torch.empty(b, s_q, 64, 512, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(b, 64, s_q, dtype=torch.float32, device="cuda")
+    p = ops.build_params(bt.q, bt.kv, bt.indices, None, None, None, None, None, 512, bt.sm_scale, out, lse)
+    tsm, ns = ops.get_mla_metadata_tensors(p, torch.device("cuda", 0), parts)
+    recs, want_ns = SO.plan(SO.row_tiles(b, s_q, topk, None), parts)
+    assert ns.cpu().tolist() == want_ns
+    assert tsm.cpu().tolist() == recs
+
+
 def test_extra_kv_sidecar():
     kc = _kc()
     spec = kc.BatchSpec(b=2, s_q=1, h_q=64, topk=256, ctx=2048, page_block=64, seed=8)
