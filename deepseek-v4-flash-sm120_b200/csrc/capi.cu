@@ -193,6 +193,15 @@ int dsv4b_get_mla_metadata(const dsv4b_decode_params* p, int num_sm_parts,
                                           static_cast<cudaStream_t>(stream)));
 }
 
+int dsv4b_plan_cluster_size(const dsv4b_decode_params* p, int num_sm_parts, int32_t* cluster_size) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (num_sm_parts <= 0 || num_sm_parts > 65535 || !cluster_size) return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((rc = current_arch_ok())) return rc;
+  *cluster_size = dsv4b::plan_cluster_size(*p, num_sm_parts);
+  return DSV4B_OK;
+}
+
 int dsv4b_sparse_decode_partial(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
                                 const int32_t* num_splits, int num_sm_parts, void* workspace,
                                 size_t workspace_bytes, void* stream) {
@@ -216,6 +225,8 @@ int dsv4b_combine(const dsv4b_decode_params* p, const int32_t* num_splits, int n
   if (!num_splits) return DSV4B_ERR_INVALID_ARGUMENT;
   WsLayout w;
   if ((rc = check_workspace(p, num_sm_parts, workspace, workspace_bytes, &w))) return rc;
+  if ((rc = current_arch_ok())) return rc;
+  if (dsv4b::plan_cluster_size(*p, num_sm_parts) > 1) return DSV4B_OK;  // merged in the clusters
   char* ws = static_cast<char*>(workspace);
   return cuda_rc(dsv4b::launch_combine(*p, num_splits, reinterpret_cast<const float*>(ws + w.lse_off),
                                        reinterpret_cast<const float*>(ws + w.o_off),
@@ -267,6 +278,7 @@ int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p, const dsv4b_sched_
                                                 reinterpret_cast<float*>(ws + w.o_off),
                                                 reinterpret_cast<int*>(ws), s))))
     return rc;
+  if (dsv4b::plan_cluster_size(*p, num_sm_parts) > 1) return DSV4B_OK;  // merged in the clusters
   return cuda_rc(dsv4b::launch_combine(*p, num_splits, reinterpret_cast<const float*>(ws + w.lse_off),
                                        reinterpret_cast<const float*>(ws + w.o_off), s));
 }

@@ -21,6 +21,11 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
 
 int decode_smem_bytes(int layout);
 
+// Cluster size of the split plan for this batch (1 = no cluster: split
+// partials go through the combine kernel).  The scheduler, the decode
+// launch and the C ABI all decide with this one function.
+int plan_cluster_size(const dsv4b_decode_params& p, int num_sm_parts);
+
 cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
                               dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream);
 

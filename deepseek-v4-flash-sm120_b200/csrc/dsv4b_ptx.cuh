@@ -101,6 +101,39 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, boo
   return r != 0;
 }
 
+// ------------------------------------------------------------- clusters
+// Every thread of every CTA in the cluster arrives (release) and waits
+// (acquire): shared-memory writes before it, local or remote, are visible
+// to every thread of the cluster after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local_saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_saddr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void dsmem_st_v4(uint32_t cluster_saddr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_saddr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
 // ------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -219,16 +252,19 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
 }
 
 // ------------------------------------------------------------- memory
+#ifndef DSV4B_LDG_QUAL
+#define DSV4B_LDG_QUAL "ld.global.L1::no_allocate"
+#endif
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile(DSV4B_LDG_QUAL ".v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint2 ldg_nc_v2(const void* p) {
   uint2 v;
-  asm volatile("ld.global.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+  asm volatile(DSV4B_LDG_QUAL ".v2.u32 {%0,%1}, [%2];"
                : "=r"(v.x), "=r"(v.y)
                : "l"(p));
   return v;

@@ -4,7 +4,10 @@
 // K2 replaces the reference's placeholder scheduler tensors
 // (csrc/api/sparse_decode.cpp:147-158, num_sm_parts = 1) with a real
 // plan: every query row r = b*s_q + s owns ceil(len/128) main tiles plus
-// ceil(extra_len/128) extra tiles.  With no more rows than parts the plan
+// ceil(extra_len/128) extra tiles.  When clusters of C >= 2 CTAs fit
+// (plan_cluster_size), row r owns the C parts of cluster r, which merge
+// the row in distributed shared memory.  Else, with no more rows than
+// parts, the plan
 // is row-aligned: t* is the smallest per-part tile cap with
 // sum_r ceil(tiles_r / t*) <= parts and row r is shared evenly by
 // ceil(tiles_r / t*) parts, so no CTA switches rows (one Q load and one
@@ -62,9 +65,20 @@ __device__ __forceinline__ int part_of_tile(long long t, long long T, long long 
   return (int)(((t + 1) * P + T - 1) / T) - 1;
 }
 
+__device__ __forceinline__ dsv4b_sched_meta empty_record() {
+  dsv4b_sched_meta m;
+  m.begin_req_idx = 0;
+  m.end_req_idx = -1;
+  m.begin_block_idx = m.end_block_idx = 0;
+  m.begin_split_idx = 0;
+  m.is_first_req_splitted = m.is_last_req_splitted = 0;
+  m.num_tiles = 0;
+  return m;
+}
+
 __global__ void __launch_bounds__(kSchedThreads)
-    sched_meta_kernel(const dsv4b_decode_params p, int num_sm_parts, dsv4b_sched_meta* sched,
-                      int32_t* num_splits) {
+    sched_meta_kernel(const dsv4b_decode_params p, int num_sm_parts, int cluster_c,
+                      dsv4b_sched_meta* sched, int32_t* num_splits) {
   // scratch first: its base stays 16-byte aligned whatever R is, so the
   // 32-entry reductions over it may be read as vectors.
   extern __shared__ __align__(16) int sh[];
@@ -87,6 +101,32 @@ __global__ void __launch_bounds__(kSchedThreads)
   __syncthreads();
   const long long T = tile_off[R];
   const int P_eff = (int)min((long long)num_sm_parts, T);
+
+  if (cluster_c > 1) {
+    // Cluster plan: row r owns parts r*C .. r*C+C-1 (one cluster), its
+    // tiles shared evenly; the cluster merges the row itself, so every row
+    // counts as one split for the combine kernel.
+    for (int r = threadIdx.x; r <= R; r += kSchedThreads) num_splits[r] = r;
+    for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+      dsv4b_sched_meta m = empty_record();
+      const int r = part / cluster_c, j = part - r * cluster_c;
+      if (r < R) {
+        const int n = tile_off[r + 1] - tile_off[r];
+        const int b0 = j * n / cluster_c, b1 = (j + 1) * n / cluster_c;
+        if (b1 > b0) {
+          m.begin_req_idx = m.end_req_idx = r;
+          m.begin_block_idx = b0;
+          m.end_block_idx = b1;
+          m.begin_split_idx = r;
+          m.is_first_req_splitted = b0 > 0;
+          m.is_last_req_splitted = b1 < n;
+          m.num_tiles = b1 - b0;
+        }
+      }
+      sched[part] = m;
+    }
+    return;
+  }
 
   if (R <= num_sm_parts) {
     // Row-aligned plan.  t* by bisection over [1, max_r tiles_r] (the
@@ -126,15 +166,8 @@ __global__ void __launch_bounds__(kSchedThreads)
     if (threadIdx.x == 0) part_off[R] = num_splits[R] = carry;
     __syncthreads();
     for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
-      dsv4b_sched_meta m;
-      if (part >= part_off[R]) {
-        m.begin_req_idx = 0;
-        m.end_req_idx = -1;
-        m.begin_block_idx = m.end_block_idx = 0;
-        m.begin_split_idx = 0;
-        m.is_first_req_splitted = m.is_last_req_splitted = 0;
-        m.num_tiles = 0;
-      } else {
+      dsv4b_sched_meta m = empty_record();
+      if (part < part_off[R]) {
         int a = 0, z = R - 1;  // the row r with part_off[r] <= part < part_off[r + 1]
         while (a < z) {
           const int mid = (a + z + 1) >> 1;
@@ -177,15 +210,8 @@ __global__ void __launch_bounds__(kSchedThreads)
 
   // 3. one record per part
   for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
-    dsv4b_sched_meta m;
-    if (part >= P_eff) {
-      m.begin_req_idx = 0;
-      m.end_req_idx = -1;
-      m.begin_block_idx = m.end_block_idx = 0;
-      m.begin_split_idx = 0;
-      m.is_first_req_splitted = m.is_last_req_splitted = 0;
-      m.num_tiles = 0;
-    } else {
+    dsv4b_sched_meta m = empty_record();
+    if (part < P_eff) {
       const long long t0 = (long long)part * T / P_eff;
       const long long t1 = (long long)(part + 1) * T / P_eff;  // exclusive, > t0
       // row containing tile x: largest r with tile_off[r] <= x
@@ -327,7 +353,8 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  sched_meta_kernel<<<1, kSchedThreads, smem, stream>>>(p, num_sm_parts, sched, num_splits);
+  sched_meta_kernel<<<1, kSchedThreads, smem, stream>>>(p, num_sm_parts, plan_cluster_size(p, num_sm_parts),
+                                                        sched, num_splits);
   return cudaGetLastError();
 }
 

@@ -47,18 +47,18 @@
 namespace dsv4b {
 
 #ifdef DSV4B_TRACE
-// Debug-build phase trace (never in the shipped library).  Each traced role
-// writes (clock64 | event | arg) words into the CTA's epilogue staging tile
-// (so no global memory traffic enters the pipeline; final-output epilogues
-// overwrite it, which the traced configurations do not use) and the log is
-// copied out at kernel end, read back with dsv4b_debug_trace_read().
-__device__ unsigned long long g_trace[4 * 3 * 128];
+// Debug-build phase trace (never in the shipped library).  The recording
+// thread of each role writes (clock64 | event | arg) words with plain
+// global stores for the first kTraceCtas CTAs of head group 0; the log is
+// read back with dsv4b_debug_trace_read().
+constexpr int kTraceCtas = 8;
+__device__ unsigned long long g_trace[kTraceCtas * 3 * 128];
 __shared__ unsigned long long* s_trace_base;
 __shared__ int s_trace_n[3];
 #define DSV4B_TR_ROLE(role, ev, a)                                                        \
   do {                                                                                    \
     const int k_ = s_trace_n[role]++;                                                     \
-    if (k_ < 128)                                                                         \
+    if (s_trace_base && k_ < 128)                                                         \
       s_trace_base[(role) * 128 + k_] =                                                   \
           ((unsigned long long)clock64() << 24) | ((ev) << 16) | ((unsigned)(a) & 0xFFFFu); \
   } while (0)
@@ -96,7 +96,7 @@ struct Misc {
   uint32_t tmem_base;
   int abort;
   uint32_t sink_word;  // target of the producers' load-completion fold
-  int pad[1];
+  uint32_t cl_live;    // cluster epilogue: bit i = cluster rank i holds a partial
   alignas(16) float red[4][64];
   alignas(16) float m_use[64];    // read as float4
   alignas(16) float alpha[64];
@@ -123,6 +123,10 @@ struct SmemPlan {
 static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kMiscOff % 1024 == 0 &&
                   SmemPlan<DSV4B_LAYOUT_MODEL1>::kMiscOff % 1024 == 0,
               "Misc must be 1024-byte aligned");
+// The cluster merge receives 512 dims x 64 heads fp32 (128 KB) in the K slots.
+static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kMiscOff - SmemPlan<DSV4B_LAYOUT_V32>::kSlotOff >= 131072 &&
+                  SmemPlan<DSV4B_LAYOUT_MODEL1>::kMiscOff - SmemPlan<DSV4B_LAYOUT_MODEL1>::kSlotOff >= 131072,
+              "cluster receive area");
 static_assert(SmemPlan<DSV4B_LAYOUT_V32>::kBytes <= 232448, "V32 smem plan too large");
 static_assert(SmemPlan<DSV4B_LAYOUT_MODEL1>::kBytes <= 232448, "MODEL1 smem plan too large");
 
@@ -197,22 +201,6 @@ __device__ __forceinline__ void load_phase_a(int q, ProdRegs<L>& R) {
 }
 
 template <int L>
-__device__ __forceinline__ void prefetch_rows_l2(int q, const ProdRegs<L>& R) {
-  if (q != 0) return;
-#pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k) {
-    const RowSrc& r = R.rs[k];
-    if (!r.valid) continue;
-    if constexpr (L == DSV4B_LAYOUT_V32) {
-      prefetch_l2_bulk(r.rec, LayoutT<L>::kRecordBytes);
-    } else {
-      prefetch_l2_bulk(r.rec, LayoutT<L>::kRowBytes);
-      prefetch_l2_bulk(reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(r.scl) & ~uintptr_t(15)), 16);
-    }
-  }
-}
-
-template <int L>
 __device__ __forceinline__ void load_phase_b(int q, ProdRegs<L>& R) {
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) {
@@ -283,13 +271,30 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   if (!cur.valid) return;
   TileCursor nxt = cursor_next(p, sm, cur);
 
+  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks.
+  auto issue_q = [&](const TileCursor& c) {
+    const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
+                              (int64_t)c.ri.b * p.stride_q_b + (int64_t)c.ri.s * p.stride_q_s;
+    for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
+      const int j = i / (NCH * 8);
+      const int rem = i - j * (NCH * 8);
+      const int ch = rem >> 3, u = rem & 7;
+      const int head = g * kHeadsPerCta + j;
+      const bool ok = head < p.h_q;
+      cp_async_16(q_s + ch * kQChunkBytes + sw128_off(j, u),
+                  qb + (ok ? (int64_t)head * p.stride_q_h + ch * 64 + u * 8 : 0), ok ? 16u : 0u);
+    }
+  };
+  // The first row's Q^T is in flight together with the first tile's loads.
+  issue_q(cur);
+
   ProdRegs<L> R;
   int idx[kRowsPerThread];
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
   rows_of<L>(p, cur, idx, R);
-  prefetch_rows_l2<L>(q, R);
   load_phase_a<L>(q, R);
+  load_phase_b<L>(q, R);
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nxt.valid ? producer_index(p, nxt, row0 + 4 * k) : -1;
   land_phase_a<L>(R, idx, M);
@@ -299,17 +304,9 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   while (cur.valid) {
     if (cur.t == cur.t_lo) {
       // New query row: (re)load Q^T once the previous row's last QK^T is done.
-      if (seg_count > 0 && !mbar_wait(&M.q_empty, (seg_count - 1) & 1, abort_flag, err)) return;
-      const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
-                                (int64_t)cur.ri.b * p.stride_q_b + (int64_t)cur.ri.s * p.stride_q_s;
-      for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
-        const int j = i / (NCH * 8);
-        const int rem = i - j * (NCH * 8);
-        const int c = rem >> 3, u = rem & 7;
-        const int head = g * kHeadsPerCta + j;
-        const bool ok = head < p.h_q;
-        cp_async_16(q_s + c * kQChunkBytes + sw128_off(j, u),
-                    qb + (ok ? (int64_t)head * p.stride_q_h + c * 64 + u * 8 : 0), ok ? 16u : 0u);
+      if (seg_count > 0) {
+        if (!mbar_wait(&M.q_empty, (seg_count - 1) & 1, abort_flag, err)) return;
+        issue_q(cur);
       }
       cp_async_wait_all();
       fence_proxy_async_smem();
@@ -332,7 +329,12 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
       mbar_arrive(&M.full[2 * m + 1]);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
     }
-    load_phase_b<L>(q, R);
+    if constexpr (LayoutT<L>::kPInRopeSlot) {
+      // V32 RoPE chunk: issued here so it lands while pairs 2, 3 are stored.
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k)
+        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
+    }
     // pairs 2, 3 (phase B registers)
 #pragma unroll
     for (int m = 2; m < 4; ++m) {
@@ -355,10 +357,6 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     }
     if constexpr (LayoutT<L>::kPInRopeSlot) {
       // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
-      // Its loads (L2 hits) overlap the wait for the previous PV.
-#pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k)
-        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
       if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
       const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
 #pragma unroll
@@ -372,8 +370,8 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     const TileCursor nn = cursor_next(p, sm, nxt);
     if (nxt.valid) {
       rows_of<L>(p, nxt, idx, R);
-      prefetch_rows_l2<L>(q, R);
       load_phase_a<L>(q, R);
+      load_phase_b<L>(q, R);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
       land_phase_a<L>(R, idx, M);
@@ -653,10 +651,29 @@ __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uin
   return exceed && row_scale != 0.0f;
 }
 
+// Cluster plan: instead of the epilogue, publish this CTA's per-head
+// stabiliser (red[1]) and row sum (red[2]) for the cluster merge.
+__device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& M) {
+  const int st = threadIdx.x - kProducerThreads;
+  if ((st >> 5) == 0) {
+#pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float lv[16];
+      tmem_ld16(tl + kColL + 16 * c16, lv);
+      tc_wait_ld();
+      if (st == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) M.red[2][16 * c16 + j] = lv[j];
+      }
+    }
+  }
+  if (st < 64) M.red[1][st] = m_run;
+}
+
 template <int L>
 __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                             const int32_t* num_splits, float* lse_accum, float* o_accum,
-                            uint32_t p_s, uint32_t tmem, Misc& M, int* err) {
+                            uint32_t p_s, uint32_t tmem, Misc& M, int* err, int cluster_c) {
   const int st = threadIdx.x - kProducerThreads;  // 0..127 = token row = TMEM lane
   const int q = st >> 5;
   const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
@@ -666,6 +683,10 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
   TileCursor cur = cursor_begin(p, sm);
   int tile_count = 0, seg_count = 0;
   float m_run = -INFINITY;  // stabiliser of head `st` (threads 0..63), log2 units
+  if (cluster_c > 1 && !cur.valid && st < 64) {  // a cluster rank with no tiles
+    M.red[1][st] = -INFINITY;
+    M.red[2][st] = 0.0f;
+  }
   while (cur.valid) {
     const bool seg_first = cur.t == cur.t_lo;
     const bool seg_last = cur.t + 1 == cur.t_hi;
@@ -699,6 +720,10 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
       if (!mbar_wait(&M.o_full, seg_count & 1, abort_flag, err)) return;
       if (st == 0) DSV4B_TR_ROLE(2, 24, seg_count);
       tc_fence_after();
+      if (cluster_c > 1) {
+        publish_partial(tl, m_run, M);
+        return;  // a cluster CTA owns one segment; the merge follows the role loops
+      }
       epilogue(p, sm, g, cur, m_run, num_splits, lse_accum, o_accum, tl, M);
       named_bar_sync(1, kSoftmaxThreads);  // staging tile reads done
       fill_ones(M, st);
@@ -711,11 +736,160 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
   }
 }
 
+// Cluster merge of one query row over the C = cluster_c CTAs that split
+// it (cluster ranks 0..C-1; rank i holds m_i, l_i per head in red[1],
+// red[2] and its unnormalised O_i^T in TMEM).  With M = max_i m_i and
+// L = sum_i l_i 2^(m_i - M): out = sum_i (2^(m_i - M) / L) O_i, then the
+// sink epilogue (tests/reference.py:124-129), lse = (M + log2 L) ln 2.
+// Rank j owns dims [j*512/C, (j+1)*512/C): every other rank stores its
+// weighted O for those dims into rank j's K-slot region (free once every
+// rank's PV is done) through distributed shared memory, as fp32
+// [sender][head quad][dim][4 heads], so a warp's 32 consecutive dims
+// write and read 512 contiguous bytes; rank j adds its own part from TMEM
+// and writes bf16.
+// Every thread of the CTA calls this; all waits before it are bounded, so
+// every CTA of the cluster reaches both cluster barriers.
+__device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uint32_t tmem,
+                                 uint32_t recv_s, Misc& M) {
+  const bool softmax = threadIdx.x >= kProducerThreads && threadIdx.x < kProducerThreads + kSoftmaxThreads;
+  const int st = threadIdx.x - kProducerThreads;
+  const uint32_t self = cluster_ctarank();
+  const int D = kDv / C;
+  const uint32_t blk_bytes = (uint32_t)D * 256u;  // one sender block: D dims x 64 heads x fp32
+  const uint32_t tl = tmem + ((uint32_t)((st >> 5) * 32) << 16);
+  const int row = blockIdx.x / C;
+  const int rb = row / p.s_q, rs = row - rb * p.s_q;
+
+  if (st == 0) DSV4B_TR_ROLE(2, 30, 0);
+  cluster_sync_all();  // 1: every rank's (m, l) is published and its PV is done
+  if (st == 0) DSV4B_TR_ROLE(2, 31, 0);
+  if (softmax) {
+    if (st < 64) {
+      float mi[8], li[8];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mi[i] = -INFINITY;
+        li[i] = 0.0f;
+        if (i < C) {
+          mi[i] = dsmem_ld_f32(dsmem_addr(smem_u32(&M.red[1][st]), i));
+          li[i] = dsmem_ld_f32(dsmem_addr(smem_u32(&M.red[2][st]), i));
+          if (li[i] > 0.0f) mx = fmaxf(mx, mi[i]);
+        }
+      }
+      float l = 0.0f;
+      uint32_t live = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (li[i] > 0.0f) {
+          l += li[i] * fast_exp2(mi[i] - mx);
+          live |= 1u << i;
+        }
+      float w = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i == (int)self && li[i] > 0.0f) w = fast_exp2(mi[i] - mx) / l;
+      const int head = g * kHeadsPerCta + st;
+      float lse = (mx + log2f(l)) * kLn2;
+      if (head < p.h_q) {
+        if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, w);
+        if (self == 0) p.lse[((int64_t)rb * p.h_q + head) * p.s_q + rs] = lse;
+      } else {
+        w = 0.0f;
+      }
+      M.scale_o[st] = w;
+      if (st == 0) M.cl_live = live;
+    }
+    named_bar_sync(1, kSoftmaxThreads);
+    const uint32_t live = M.cl_live;
+    if (live & (1u << self)) {
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + st;
+        const int owner = d / D, dl = d - owner * D;
+        const uint32_t dst = dsmem_addr(recv_s + self * blk_bytes + (uint32_t)dl * 16u, owner);
+#pragma unroll
+        for (int hg = 0; hg < 4; ++hg) {
+          float ov[16];
+          tmem_ld16(tl + kColO + 64 * m + 16 * hg, ov);
+          tc_wait_ld();
+          if (owner != (int)self) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 w4 = *reinterpret_cast<const float4*>(&M.scale_o[16 * hg + 4 * k]);
+              dsmem_st_v4(dst + (uint32_t)(4 * hg + k) * (uint32_t)D * 16u, ov[4 * k] * w4.x, ov[4 * k + 1] * w4.y, ov[4 * k + 2] * w4.z,
+                          ov[4 * k + 3] * w4.w);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (st == 0) DSV4B_TR_ROLE(2, 32, 0);
+  cluster_sync_all();  // 2: every rank's contribution has landed at its owner
+  if (st == 0) DSV4B_TR_ROLE(2, 33, 0);
+  if (!softmax) return;
+  const uint32_t live = M.cl_live;
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)rb * p.stride_o_b +
+                       (int64_t)rs * p.stride_o_s;
+  const int lo = (int)self * D, hi = lo + D;
+  const int r = st >> 2, part = st & 3;
+#pragma unroll 1
+  for (int m = lo / 128; m * 128 < hi; ++m) {
+    const int d = 128 * m + st;
+    const bool mine = d >= lo && d < hi;  // uniform per warp (D >= 64)
+    const int dl = d - lo;
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+      if (mine) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float acc[16];
+          tmem_ld16(tl + kColO + 64 * m + 32 * hf + 16 * c, acc);
+          tc_wait_ld();
+          const bool own = (live >> self) & 1u;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = own ? acc[j] * M.scale_o[32 * hf + 16 * c + j] : 0.0f;
+#pragma unroll 1
+          for (int i = 0; i < C; ++i) {
+            if (i == (int)self || !((live >> i) & 1u)) continue;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t u = (uint32_t)(8 * hf + 4 * c + k);
+              float4 v;
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                           : "r"(recv_s + (uint32_t)i * blk_bytes + (u * (uint32_t)D + (uint32_t)dl) * 16u));
+              acc[4 * k] += v.x;
+              acc[4 * k + 1] += v.y;
+              acc[4 * k + 2] += v.z;
+              acc[4 * k + 3] += v.w;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) M.stage[16 * c + j][st] = __float2bfloat16_rn(acc[j]);
+        }
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+      const int head = g * kHeadsPerCta + 32 * hf + r;
+      const int dq = 128 * m + 32 * part;
+      if (head < p.h_q && dq >= lo && dq < hi) {
+        uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)head * p.stride_o_h + dq);
+        const uint4* src = reinterpret_cast<const uint4*>(&M.stage[r][32 * part]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = src[k];
+      }
+      named_bar_sync(1, kSoftmaxThreads);
+    }
+  }
+  if (st == 0) DSV4B_TR_ROLE(2, 34, 0);
+}
+
 template <int L>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_decode_kernel(const dsv4b_decode_params p, const dsv4b_sched_meta* __restrict__ sched,
                          const int32_t* __restrict__ num_splits, float* __restrict__ lse_accum,
-                         float* __restrict__ o_accum, int* __restrict__ err) {
+                         float* __restrict__ o_accum, int* __restrict__ err, int cluster_c) {
   using SP = SmemPlan<L>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -741,8 +915,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     M.abort = 0;
 #ifdef DSV4B_TRACE
     s_trace_n[0] = s_trace_n[1] = s_trace_n[2] = 0;
-    s_trace_base = reinterpret_cast<unsigned long long*>(&M.stage[0][0]);
-    for (int i = 0; i < 3 * 128; ++i) s_trace_base[i] = 0;
+    s_trace_base = (blockIdx.x < kTraceCtas && blockIdx.y == 0) ? g_trace + blockIdx.x * 3 * 128 : nullptr;
+    if (s_trace_base) {
+      for (int i = 0; i < 3 * 128; ++i) s_trace_base[i] = 0;
+      s_trace_base[0] = (unsigned long long)clock64() << 24;  // role 0 slot 0: kernel start
+      s_trace_n[0] = 1;
+      unsigned long long gt;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+      s_trace_base[127] = gt;  // role 0 last slot: globaltimer at start
+      s_trace_base[126] = (unsigned long long)clock64();
+    }
 #endif
     fence_mbarrier_init();
   }
@@ -759,44 +941,122 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kProducerWarps) {
     run_producer<L>(p, sm, g, q_s, slot_s, M, err);
   } else if (warp < kMmaWarp) {
-    run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, p_s, tmem, M, err);
+    run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, p_s, tmem, M, err, cluster_c);
   } else if (lane == 0) {
     run_mma<L>(p, sm, q_s, slot_s, p_s, tmem, M, err);
   }
 
   tc_fence_before();
   __syncthreads();
+  if (cluster_c > 1) {
+    tc_fence_after();
+    cluster_epilogue(p, g, cluster_c, tmem, slot_s, M);
+    tc_fence_before();
+    __syncthreads();
+  }
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
 #ifdef DSV4B_TRACE
-  if (blockIdx.x < 4 && blockIdx.y == 0)
-    for (int i = threadIdx.x; i < 3 * 128; i += blockDim.x) g_trace[blockIdx.x * 3 * 128 + i] = s_trace_base[i];
+  if (threadIdx.x == 0 && s_trace_base) {
+    unsigned long long gt;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+    s_trace_base[255] = gt;  // role 1 last slot: globaltimer at end
+    s_trace_base[254] = (unsigned long long)clock64();
+  }
 #endif
 }
 
 template <int L>
-cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
-                               const int32_t* num_splits, int num_sm_parts, float* lse_accum,
-                               float* o_accum, int* err, cudaStream_t stream) {
-  constexpr int smem = SmemPlan<L>::kBytes;
+cudaError_t set_smem_attr() {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_done[dev]) {
-    e = cudaFuncSetAttribute(sparse_decode_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(sparse_decode_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SmemPlan<L>::kBytes);
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  const dim3 grid(num_sm_parts, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta);
-  sparse_decode_kernel<L><<<grid, kThreads, smem, stream>>>(p, sched, num_splits, lse_accum, o_accum, err);
-  return cudaGetLastError();
+  return cudaSuccess;
+}
+
+// Whether clusters of c decode CTAs can be resident at all on this device
+// (one CTA per SM, clusters confined to a GPC).  Cached per device.
+template <int L>
+bool cluster_fits(int c) {
+  static signed char cache[64][4] = {};  // 0 unknown, 1 yes, -1 no; index log2(c) - 1
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const int k = c == 2 ? 0 : c == 4 ? 1 : 2;
+  if (cache[dev][k] == 0) {
+    bool ok = set_smem_attr<L>() == cudaSuccess;
+    if (ok) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(c, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = SmemPlan<L>::kBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = c;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      ok = cudaOccupancyMaxActiveClusters(&n, sparse_decode_kernel<L>, &cfg) == cudaSuccess && n >= 1;
+      cudaGetLastError();  // a refused query leaves no sticky error
+    }
+    cache[dev][k] = ok ? 1 : -1;
+  }
+  return cache[dev][k] > 0;
+}
+
+template <int L>
+cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                               const int32_t* num_splits, int num_sm_parts, float* lse_accum,
+                               float* o_accum, int* err, cudaStream_t stream) {
+  cudaError_t e = set_smem_attr<L>();
+  if (e != cudaSuccess) return e;
+  const int c = plan_cluster_size(p, num_sm_parts);
+  const int groups = (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c > 1 ? p.b * p.s_q * c : num_sm_parts, groups, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = SmemPlan<L>::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = c > 1 ? c : 1;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = c > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, sparse_decode_kernel<L>, p, sched, num_splits, lse_accum, o_accum, err,
+                            c > 1 ? c : 1);
 }
 
 }  // namespace
+
+// Cluster size of the plan for this batch: the largest power of two C <= 8
+// with b*s_q*C <= num_sm_parts and C <= the most tiles a query row can
+// have, whose clusters fit on the device; 1 = no cluster (split partials
+// are merged by the combine kernel instead).
+int plan_cluster_size(const dsv4b_decode_params& p, int num_sm_parts) {
+  const int64_t rows = (int64_t)p.b * p.s_q;
+  const int tiles_max = (p.topk + kTileTokens - 1) / kTileTokens +
+                        (p.extra_kv ? (p.extra_topk + kTileTokens - 1) / kTileTokens : 0);
+  for (int c = 8; c >= 2; c >>= 1) {
+    if (rows * c > num_sm_parts || c > tiles_max) continue;
+    const bool fits = p.layout == DSV4B_LAYOUT_V32 ? cluster_fits<DSV4B_LAYOUT_V32>(c)
+                                                   : cluster_fits<DSV4B_LAYOUT_MODEL1>(c);
+    if (fits) return c;
+  }
+  return 1;
+}
 
 cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
                                  const int32_t* num_splits, int num_sm_parts, float* lse_accum,
@@ -810,7 +1070,7 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
 
 #ifdef DSV4B_TRACE
 extern "C" DSV4B_API int dsv4b_debug_trace_read(unsigned long long* dst, int max_words) {
-  const int n = 4 * 3 * 128 < max_words ? 4 * 3 * 128 : max_words;
+  const int n = kTraceCtas * 3 * 128 < max_words ? kTraceCtas * 3 * 128 : max_words;
   cudaMemcpyFromSymbol(dst, g_trace, n * sizeof(unsigned long long));
   return n;
 }

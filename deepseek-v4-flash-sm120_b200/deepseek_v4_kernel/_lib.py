@@ -31,6 +31,7 @@ EXPORTED = (
     "dsv4b_num_sm_parts", "dsv4b_workspace_bytes", "dsv4b_get_mla_metadata",
     "dsv4b_sparse_decode", "dsv4b_combine", "dsv4b_sparse_decode_partial",
     "dsv4b_gather_dequant", "dsv4b_read_kernel_status", "dsv4b_sparse_decode_noalloc",
+    "dsv4b_plan_cluster_size",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -83,6 +84,7 @@ def _load():
     lib.dsv4b_workspace_bytes.argtypes = [ctypes.c_int] * 4
     P = ctypes.POINTER(DecodeParams)
     lib.dsv4b_get_mla_metadata.argtypes = [P, ctypes.c_int, _vp, _vp, _vp]
+    lib.dsv4b_plan_cluster_size.argtypes = [P, ctypes.c_int, ctypes.POINTER(_i32)]
     for fn in (lib.dsv4b_sparse_decode, lib.dsv4b_sparse_decode_partial):
         fn.argtypes = [P, _vp, _vp, ctypes.c_int, _vp, ctypes.c_size_t, _vp]
     lib.dsv4b_combine.argtypes = [P, _vp, ctypes.c_int, _vp, ctypes.c_size_t, _vp]

@@ -155,6 +155,13 @@ def build_params(q, kv, indices, topk_length, attn_sink, extra_kv, extra_indices
     return p
 
 
+def plan_cluster_size(p: DecodeParams, parts: int) -> int:
+    """Cluster size of the tile plan for these shapes (1 = no cluster)."""
+    c = ctypes.c_int32()
+    check("dsv4b_plan_cluster_size", lib.dsv4b_plan_cluster_size(ctypes.byref(p), parts, ctypes.byref(c)))
+    return int(c.value)
+
+
 def get_mla_metadata_tensors(p: DecodeParams, device: torch.device,
                              parts: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Run the on-device scheduler (K2); returns (tile_scheduler_metadata

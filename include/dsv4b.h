@@ -132,6 +132,17 @@ DSV4B_API int dsv4b_get_mla_metadata(const dsv4b_decode_params* p, int num_sm_pa
                            dsv4b_sched_meta* sched_meta, int32_t* num_splits,
                            void* stream);
 
+/* Cluster size of the tile plan dsv4b_get_mla_metadata makes for these
+ * shapes and num_sm_parts (a pure function of b*s_q, topk, extra_topk,
+ * the layout and the device).  C >= 2: each query row is split over the C
+ * CTAs of one thread-block cluster, which merge the row in distributed
+ * shared memory, so the combine kernel has nothing to do and
+ * num_splits = [0, 1, ..., b*s_q]; 1: split rows are merged by
+ * dsv4b_combine().  Part of the get_mla_metadata protocol it extends
+ * (flash_mla_interface.py:38-51); the reference has no split plan. */
+DSV4B_API int dsv4b_plan_cluster_size(const dsv4b_decode_params* p, int num_sm_parts,
+                                      int32_t* cluster_size);
+
 /* Sparse decode forward: decode kernel (K1) plus split combine (K3).
  * Replaces dsv4_kernel::sparse_decode_fwd (csrc/api/sparse_decode.cpp:29-172)
  * and sm120::launch_dsv4_sparse_decode_v32

@@ -9,6 +9,11 @@ ceil(len_main/128) + ceil(len_extra/128) tiles, len_main =
 max(min(topk_length[b], topk), 1) (tests/reference.py:107-109),
 len_extra = clamp(extra_topk_length[b], 0, extra_topk).
 
+* cluster size C >= 2 (chosen by the library from the shapes, the layout
+  and the device: dsv4b_plan_cluster_size): row r owns parts r*C + j,
+  j < C, with tiles [floor(j*n/C), floor((j+1)*n/C)) (empty ranges give the
+  empty record); num_splits = [0, 1, ..., R] since each cluster merges its
+  row itself.
 * R <= num_sm_parts (row-aligned): t* = the smallest per-part tile cap with
   sum_r ceil(tiles_r / t*) <= num_sm_parts; row r gets k_r =
   ceil(tiles_r / t*) consecutive parts and its part j covers tiles
@@ -67,9 +72,28 @@ def _plan_row_aligned(tiles: Sequence[int], num_sm_parts: int):
     return recs, ns
 
 
-def plan(tiles: Sequence[int], num_sm_parts: int) -> Tuple[List[List[int]], List[int]]:
+def _plan_cluster(tiles: Sequence[int], num_sm_parts: int, c: int):
+    R = len(tiles)
+    recs = []
+    for part in range(num_sm_parts):
+        r, j = divmod(part, c)
+        rec = list(EMPTY)
+        if r < R:
+            n = tiles[r]
+            bb, eb = j * n // c, (j + 1) * n // c
+            if eb > bb:
+                rec = [r, r, bb, eb, r, int(bb > 0), int(eb < n), eb - bb]
+        recs.append(rec)
+    return recs, list(range(R + 1))
+
+
+def plan(tiles: Sequence[int], num_sm_parts: int,
+         cluster: int = 1) -> Tuple[List[List[int]], List[int]]:
     """Returns (records [num_sm_parts][8], num_splits [R+1])."""
     R = len(tiles)
+    if cluster > 1:
+        assert R * cluster <= num_sm_parts
+        return _plan_cluster(tiles, num_sm_parts, cluster)
     if R <= num_sm_parts:
         return _plan_row_aligned(tiles, num_sm_parts)
     off = [0]

@@ -14,8 +14,8 @@ import pytest
 from oracle import schedule_oracle as SO
 
 
-def _check_plan(tiles, parts):
-    recs, ns = SO.plan(tiles, parts)
+def _check_plan(tiles, parts, cluster=1):
+    recs, ns = SO.plan(tiles, parts, cluster)
     R = len(tiles)
     assert len(recs) == parts and len(ns) == R + 1 and ns[0] == 0
     covered = {r: [] for r in range(R)}   # row -> [(begin, end, split)]
@@ -41,9 +41,11 @@ def _check_plan(tiles, parts):
         for (a0, a1, _), (b0, _, _) in zip(segs, segs[1:]):
             assert a1 == b0
         # a row covered by k parts owns splits ns[r] .. ns[r]+k-1
-        assert ns[r + 1] - ns[r] == len(segs)
+        if cluster == 1:
+            assert ns[r + 1] - ns[r] == len(segs)
         firsts = [s for lo, _, s in segs]
-        assert firsts == list(range(ns[r], ns[r + 1])) or len(segs) == 1
+        if cluster == 1:
+            assert firsts == list(range(ns[r], ns[r + 1])) or len(segs) == 1
     return recs, ns
 
 
@@ -84,3 +86,18 @@ def test_fewer_tiles_than_parts_leaves_empty_records():
     recs, ns = _check_plan([1, 1], 148)
     assert sum(1 for r in recs if r[1] >= r[0]) == 2
     assert ns == [0, 1, 2]
+
+
+@pytest.mark.parametrize("cluster", [2, 4, 8])
+def test_cluster_plan_keeps_rows_in_their_cluster(cluster):
+    rng = random.Random(cluster)
+    tiles = [rng.randint(1, 20) for _ in range(148 // cluster)]
+    recs, ns = _check_plan(tiles, 148, cluster)
+    assert ns == list(range(len(tiles) + 1))
+    for part, rec in enumerate(recs):
+        if rec[1] >= rec[0]:
+            assert rec[0] == rec[1] == part // cluster
+    # every rank gets floor or ceil of tiles / C
+    for r, n in enumerate(tiles):
+        got = [recs[r * cluster + j][7] for j in range(cluster)]
+        assert sum(got) == n and max(got) - min(got) <= 1

@@ -22,17 +22,22 @@ def _kc():
     return kvcache
 
 
+def _params(batch, topk_length=None, extra=None):
+    from deepseek_v4_kernel import ops
+    q = batch.q
+    b, s_q, h_q, d_qk = q.shape
+    o = torch.empty(b, s_q, h_q, 512, dtype=torch.bfloat16, device=q.device)
+    l = torch.empty(b, h_q, s_q, dtype=torch.float32, device=q.device)
+    return ops.build_params(q, batch.kv, batch.indices, topk_length, batch.attn_sink,
+                            *(extra if extra else (None, None, None)), 512, batch.sm_scale, o, l)
+
+
 def _run(batch, topk_length=None, parts=None, extra=None, out=None):
     from deepseek_v4_kernel import ops
     q, kv, idx = batch.q, batch.kv, batch.indices
     tsm = ns = None
     if parts is not None:
-        b, s_q, h_q, d_qk = q.shape
-        o = torch.empty(b, s_q, h_q, 512, dtype=torch.bfloat16, device=q.device)
-        l = torch.empty(b, h_q, s_q, dtype=torch.float32, device=q.device)
-        p = ops.build_params(q, kv, idx, topk_length, batch.attn_sink,
-                             *(extra if extra else (None, None, None)), 512, batch.sm_scale, o, l)
-        tsm, ns = ops.get_mla_metadata_tensors(p, q.device, parts)
+        tsm, ns = ops.get_mla_metadata_tensors(_params(batch, topk_length, extra), q.device, parts)
     ekv, eidx, etk = extra if extra else (None, None, None)
     return ops.sparse_decode_fwd(q, kv, idx, topk_length, batch.attn_sink, tsm, ns, ekv, eidx, etk,
                                  512, batch.sm_scale, out=out)
@@ -154,7 +159,9 @@ def test_topk_length_and_zero_length():
 
 @pytest.mark.parametrize("parts", [1, 3, 7, 148, 300])
 def test_split_counts_agree(parts):
-    """Any scheduler part count gives the oracle's answer (split + combine)."""
+    """Any scheduler part count gives the oracle's answer: contiguous plan
+    + combine (1 part), row-aligned + combine (3), clusters of 2 (7) and
+    8 (148, 300) merged in distributed shared memory."""
     spec = _kc().BatchSpec(b=3, s_q=1, h_q=64, topk=1000, ctx=8192, page_block=64,
                            invalid_tail=5, seed=21)
     bt = _kc().make_batch(spec)
@@ -162,7 +169,9 @@ def test_split_counts_agree(parts):
     out, lse, tsm, ns = _run(bt, topk_length=tk, parts=parts)
     ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, tk, bt.attn_sink, bt.sm_scale, "v32")
     assert_matches(out, lse, ref_out, ref_lse)
-    recs, want_ns = SO.plan(SO.row_tiles(3, 1, 1000, tk.tolist()), parts)
+    from deepseek_v4_kernel import ops
+    c = ops.plan_cluster_size(_params(bt, tk), parts)
+    recs, want_ns = SO.plan(SO.row_tiles(3, 1, 1000, tk.tolist()), parts, c)
     assert tsm.cpu().tolist() == recs
     assert ns.cpu().tolist() == want_ns
 
@@ -181,7 +190,8 @@ def test_scheduler_records_match_oracle(b, s_q, topk, parts):
     lse = torch.empty(b, 64, s_q, dtype=torch.float32, device="cuda")
     p = ops.build_params(bt.q, bt.kv, bt.indices, None, None, None, None, None, 512, bt.sm_scale, out, lse)
     tsm, ns = ops.get_mla_metadata_tensors(p, torch.device("cuda", 0), parts)
-    recs, want_ns = SO.plan(SO.row_tiles(b, s_q, topk, None), parts)
+    c = ops.plan_cluster_size(p, parts)
+    recs, want_ns = SO.plan(SO.row_tiles(b, s_q, topk, None), parts, c)
     assert ns.cpu().tolist() == want_ns
     assert tsm.cpu().tolist() == recs
 
