@@ -13,26 +13,27 @@
 //    and the 64 heads are N.  O is computed transposed as well,
 //    O^T[dim, head] += V^T . P^T, with V^T read MN-major straight out of
 //    the same bf16 K tile (4 M-blocks of 128 dims).
-//  * TMEM (512 columns): S^T [0,64), O^T [64,320), per-thread partial
-//    softmax row sums [320,384).
+//  * TMEM (512 columns): S^T [0,64), O^T [64,320), softmax row sums
+//    [320,384) (ones[64 x 128] . P^T on the tensor core).
 //  * Shared memory: Q^T (64 heads x d_qk bf16, 72 KB for V32) and a ring of
 //    d_qk/64 chunk slots, each a 128-token x 64-column bf16 SWIZZLE_128B
 //    tile (16 KB).  PV M-block m releases slots 2m, 2m+1, so the next
 //    tile's dequant overlaps the current PV.  V32 writes P^T into the RoPE
 //    slot (RoPE is not part of V); MODEL1 has a separate P^T buffer.
 //
-// Warp roles (416 threads):
-//   warps 0-7   producers: per tile, each thread owns one token row and
-//               one 32-column half of every chunk; loads raw FP8 / scales /
-//               RoPE with 16-byte loads one tile ahead, dequantises, stores
-//               swizzled bf16; also loads Q^T at each query-row change and
-//               issues L2 bulk prefetches two tiles ahead.
+// Warp roles (384 threads):
+//   warps 0-7   producers: per tile, each thread owns four token rows and a
+//               16-byte column unit of every 128-column chunk pair; loads
+//               raw FP8 / scales / RoPE with 16-byte loads one tile ahead,
+//               dequantises, stores swizzled bf16; also loads Q^T at each
+//               query-row change.
 //   warps 8-11  softmax + epilogue: thread = token row = TMEM lane;
 //               column max via redux.sync + a 4-warp exchange, lazy
 //               rescaling (only when a head's max grows by > 2^8), P^T to
-//               shared memory, row sums in TMEM, final normalisation, sink,
-//               LSE and the output / split-partial store.
-//   warp 12     TMEM allocation and the single-thread tcgen05.mma issuer.
+//               shared memory, final normalisation, sink, LSE and the
+//               output / split-partial store (or the cluster merge).
+//               Warp 8 allocates TMEM and its lane 0 issues every
+//               tcgen05.mma, between its softmax passes.
 //
 // All mbarrier waits are bounded (dsv4b_ptx.cuh: mbar_wait); on a timeout
 // the CTA raises an abort flag, every role leaves its loop, TMEM is freed
@@ -72,10 +73,12 @@ namespace {
 
 constexpr int kProducerWarps = 8;
 constexpr int kSoftmaxWarps = 4;
-constexpr int kThreads = (kProducerWarps + kSoftmaxWarps + 1) * 32;  // 416
+// 384 threads = 3 x 128: the register allocator then grants 168 per thread
+// (a 416-thread block is allocated as 512 threads and capped at 128).
+constexpr int kThreads = (kProducerWarps + kSoftmaxWarps) * 32;  // 384
 constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
-constexpr int kMmaWarp = kProducerWarps + kSoftmaxWarps;
+constexpr int kMmaWarp = kProducerWarps;  // lane 0 of the first softmax warp issues the MMAs
 
 constexpr int kQChunkBytes = kHeadsPerCta * 128;       // 8 KB
 constexpr int kSlotBytes = kTileTokens * 128;          // 16 KB
@@ -150,22 +153,30 @@ __device__ __forceinline__ int empty_of(int c) {
 // columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
 // pair one PV M-block releases.
 //
-// Loads are split in two register phases per tile.  Phase A (pairs 0-1 and
-// the scales) is issued at the end of the previous tile together with an
-// L2 bulk prefetch of each whole row, and landed there.  Phase B (pairs 2-3
-// and MODEL1 RoPE) is issued after pairs 0-1 are stored and hits L2; the
-// V32 RoPE chunk is loaded after pair 3, while waiting for the previous PV.  A proxy fence
-// followed by an mbarrier arrive waits for all of the thread's outstanding
-// loads, so every hand-off happens with no load in flight.
-constexpr int kRowsPerThread = 4;
+// Producer groups.  Group 0 (warps 0-3) fills chunk pairs 0-1 of every
+// tile, group 1 (warps 4-7) pairs 2-3 and the RoPE chunk.  Within a group,
+// warp w owns tile rows 32w..32w+31 and handles four of them per pass: in
+// pass k lane l works on row 32w + 4k + (l >> 3) and on the 16-byte column
+// q = l & 7 of a 128-byte block of that row, so a warp load reads four
+// rows x 128 contiguous bytes (whole 32-byte sectors).  A "chunk pair" is
+// 128 columns = two 64-column SW128 chunk slots = one V32 scale tile = the
+// slot pair one PV M-block releases.
+//
+// Random 656-B rows arrive at roughly 21-25 GB/s per SM, so a tile's 84 KB
+// needs a whole tile period in flight.  The hand-off of stored slots (proxy
+// fence + mbarrier arrive) waits for every load the thread has
+// outstanding, so each group issues its share of tile t+1 right after its
+// own last hand-off of tile t: its loads then stream in during the whole
+// period until the group's next fill, and the two groups' loads are
+// staggered.
+constexpr int kGroupThreads = kProducerThreads / 2;  // 128
+constexpr int kRowsPerThread = 8;
 
 template <int L>
-struct ProdRegs {
-  RowSrc rs[kRowsPerThread];
-  uint4 fa[2][kRowsPerThread];  // phase A: pairs 0, 1
-  uint4 sc[kRowsPerThread];     // V32: 4 fp32 scales; MODEL1: 8 UE8M0 bytes in .x/.y
-  uint4 fb[2][kRowsPerThread];  // phase B: pairs 2, 3 (MODEL1 pair 3: fp8 or RoPE part 0)
-  uint4 rp[kRowsPerThread];     // V32 RoPE; MODEL1 RoPE part 1
+struct GroupRegs {
+  uint4 f[2][kRowsPerThread];  // this group's two chunk pairs (MODEL1 pair 3, q >= 4: RoPE part 0)
+  uint2 sc[kRowsPerThread];    // V32: the pairs' two fp32 scales; MODEL1: the row's 8 UE8M0 bytes
+  uint4 rp[kRowsPerThread];    // group 1: V32 RoPE; MODEL1 RoPE part 1 (q >= 4)
 };
 
 // Flat cache index of tile row r, or -1 for padding (>= the row's attended
@@ -180,64 +191,38 @@ __device__ __forceinline__ uint4 ldg_or_zero(bool ok, const uint8_t* ptr) {
   return ok ? ldg_nc_v4(ptr) : make_uint4(0, 0, 0, 0);
 }
 
+// Issues this group's loads of one tile (rows given by their flat indices).
 template <int L>
-__device__ __forceinline__ void rows_of(const dsv4b_decode_params& p, const TileCursor& c,
-                                        const int (&idx)[kRowsPerThread], ProdRegs<L>& R) {
+__device__ __forceinline__ void group_load(const dsv4b_decode_params& p, const TileCursor& c, int grp,
+                                           int q, const int (&idx)[kRowsPerThread], GroupRegs<L>& R) {
   const TileSpan ts = tile_span(p, c);
 #pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k)
-    R.rs[k] = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
-}
-
-template <int L>
-__device__ __forceinline__ void load_phase_a(int q, ProdRegs<L>& R) {
-#pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) {
-    const RowSrc& r = R.rs[k];
-    R.fa[0][k] = ldg_or_zero(r.valid, r.rec + 16 * q);
-    R.fa[1][k] = ldg_or_zero(r.valid, r.rec + 128 + 16 * q);
-    R.sc[k] = load_scales<L>(r);
-  }
-}
-
-template <int L>
-__device__ __forceinline__ void load_phase_b(int q, ProdRegs<L>& R) {
-#pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k) {
-    const RowSrc& r = R.rs[k];
-    R.fb[0][k] = ldg_or_zero(r.valid, r.rec + 256 + 16 * q);
+    const RowSrc r = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
+    const int c0 = 256 * grp;  // byte offset of this group's first pair
+    R.f[0][k] = ldg_or_zero(r.valid, r.rec + c0 + 16 * q);
     if constexpr (L == DSV4B_LAYOUT_V32) {
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
-    } else if (q < 4) {  // MODEL1 pair 3: fp8 columns 384..447 ...
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
-    } else {             // ... and the 64 bf16 RoPE columns
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
-      R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
+      R.f[1][k] = ldg_or_zero(r.valid, r.rec + c0 + 128 + 16 * q);
+      R.sc[k] = r.valid ? ldg_nc_v2(r.scl + 8 * grp) : make_uint2(0, 0);
+      if (grp == 1) R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 16 * q);
+    } else {
+      if (grp == 0 || q < 4) {
+        R.f[1][k] = ldg_or_zero(r.valid, r.rec + c0 + 128 + 16 * q);
+      } else {  // MODEL1 pair 3, lanes 4-7: the 64 bf16 RoPE columns
+        R.f[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
+        R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
+      }
+      R.sc[k] = r.valid ? ldg_nc_v2(r.scl) : make_uint2(0, 0);
     }
   }
 }
 
-// Folds registers into one word stored to shared memory: pins the loads
-// (and their completion) to this point, so the code generator cannot sink
-// them into the chunk loop where the latency would be exposed per chunk.
+// Scale of the 16 columns lane q holds in chunk pair m (j = m & 1 within
+// the group).
 template <int L>
-__device__ __forceinline__ void land_phase_a(const ProdRegs<L>& R, const int (&idx)[kRowsPerThread],
-                                             Misc& M) {
-  uint32_t x = 0;
-#pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k) {
-    x ^= R.fa[0][k].x ^ R.fa[0][k].y ^ R.fa[0][k].z ^ R.fa[0][k].w;
-    x ^= R.fa[1][k].x ^ R.fa[1][k].y ^ R.fa[1][k].z ^ R.fa[1][k].w;
-    x ^= R.sc[k].x ^ R.sc[k].y ^ R.sc[k].z ^ R.sc[k].w ^ (uint32_t)idx[k];
-  }
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(&M.sink_word)), "r"(x) : "memory");
-}
-
-// Scale of the 16 columns lane q holds in chunk pair m.
-template <int L>
-__device__ __forceinline__ float pair_scale(const uint4& sc, int m, int q) {
+__device__ __forceinline__ float pair_scale(const uint2& sc, int m, int q) {
   if constexpr (L == DSV4B_LAYOUT_V32) {
-    return __uint_as_float(m == 0 ? sc.x : m == 1 ? sc.y : m == 2 ? sc.z : sc.w);
+    return __uint_as_float((m & 1) ? sc.y : sc.x);
   } else {
     const int byte = 2 * m + (q >> 2);  // 64-column UE8M0 tiles
     const uint32_t w = byte < 4 ? sc.x : sc.y;
@@ -263,15 +248,18 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   using LT = LayoutT<L>;
   constexpr int NCH = LT::kChunks;
   const int ptid = threadIdx.x;
-  const int w = ptid >> 5, lane = ptid & 31;
+  const int grp = ptid / kGroupThreads;
+  const int gt = ptid - grp * kGroupThreads;
+  const int w = gt >> 5, lane = gt & 31;
   const int q = lane & 7;
-  const int row0 = 16 * w + (lane >> 3);  // row of pass k: row0 + 4k
+  const int row0 = 32 * w + (lane >> 3);  // row of pass k: row0 + 4k
 
   TileCursor cur = cursor_begin(p, sm);
   if (!cur.valid) return;
   TileCursor nxt = cursor_next(p, sm, cur);
 
-  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks.
+  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks
+  // (all 256 producer threads).
   auto issue_q = [&](const TileCursor& c) {
     const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
                               (int64_t)c.ri.b * p.stride_q_b + (int64_t)c.ri.s * p.stride_q_s;
@@ -288,16 +276,13 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   // The first row's Q^T is in flight together with the first tile's loads.
   issue_q(cur);
 
-  ProdRegs<L> R;
+  GroupRegs<L> R;
   int idx[kRowsPerThread];
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
-  rows_of<L>(p, cur, idx, R);
-  load_phase_a<L>(q, R);
-  load_phase_b<L>(q, R);
+  group_load<L>(p, cur, grp, q, idx, R);
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nxt.valid ? producer_index(p, nxt, row0 + 4 * k) : -1;
-  land_phase_a<L>(R, idx, M);
 
   int tile_count = 0, seg_count = 0;
   volatile int* abort_flag = &M.abort;
@@ -317,64 +302,45 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     if (ptid == 0) DSV4B_TR_ROLE(0, 1, tile_count);
     const uint32_t wait_par = (tile_count - 1) & 1;
 
-    // pairs 0, 1 (phase A registers)
 #pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
-#pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k)
-        store_pair_fp8(slot_s, m, row0 + 4 * k, q, R.fa[m][k], pair_scale<L>(R.sc[k], m, q));
-      fence_proxy_async_smem();
-      mbar_arrive(&M.full[2 * m]);
-      mbar_arrive(&M.full[2 * m + 1]);
-      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
-    }
-    if constexpr (LayoutT<L>::kPInRopeSlot) {
-      // V32 RoPE chunk: issued here so it lands while pairs 2, 3 are stored.
-#pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k)
-        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
-    }
-    // pairs 2, 3 (phase B registers)
-#pragma unroll
-    for (int m = 2; m < 4; ++m) {
+    for (int j = 0; j < 2; ++j) {
+      const int m = 2 * grp + j;
       if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) {
         const int row = row0 + 4 * k;
         if (L == DSV4B_LAYOUT_MODEL1 && m == 3 && q >= 4) {
           const uint32_t slot = slot_s + 7 * kSlotBytes;  // MODEL1 RoPE chunk
-          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.fb[1][k]);
+          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.f[1][k]);
           sts_v4(slot + sw128_off(row, 2 * (q - 4) + 1), R.rp[k]);
         } else {
-          store_pair_fp8(slot_s, m, row, q, R.fb[m - 2][k], pair_scale<L>(R.sc[k], m, q));
+          store_pair_fp8(slot_s, m, row, q, R.f[j][k], pair_scale<L>(R.sc[k], m, q));
         }
       }
       fence_proxy_async_smem();
       mbar_arrive(&M.full[2 * m]);
       mbar_arrive(&M.full[2 * m + 1]);
-      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+      if (gt == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
     }
     if constexpr (LayoutT<L>::kPInRopeSlot) {
-      // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
-      if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
-      const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
+      if (grp == 1) {
+        // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
+        if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
+        const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
 #pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
-      fence_proxy_async_smem();
-      mbar_arrive(&M.full[NCH - 1]);
-      if (ptid == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
+        for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
+        fence_proxy_async_smem();
+        mbar_arrive(&M.full[NCH - 1]);
+        if (gt == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
+      }
     }
 
-    // batch: phase A of the next tile, indices of the one after
+    // This group's loads of the next tile, then the indices of the one after.
     const TileCursor nn = cursor_next(p, sm, nxt);
     if (nxt.valid) {
-      rows_of<L>(p, nxt, idx, R);
-      load_phase_a<L>(q, R);
-      load_phase_b<L>(q, R);
+      group_load<L>(p, nxt, grp, q, idx, R);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
-      land_phase_a<L>(R, idx, M);
     }
     if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
@@ -385,68 +351,73 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
 }
 
 // ------------------------------------------------------------- MMA issuer
+// One thread (lane 0 of the first softmax warp) issues every tcgen05.mma,
+// between that warp's softmax passes: QK^T of tile t+1 follows PV of tile
+// t, which follows the softmax of tile t, so no MMA is delayed by sharing
+// the warp.
+struct MmaState {
+  int tile_count = 0, seg_count = 0;
+};
+
+// S^T[128 tok, 64 heads] = K_tile[128, d_qk] . Q^T (K-major A and B), chunk
+// by chunk as the producers land them.
 template <int L>
-__device__ void run_mma(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, uint32_t q_s,
-                        uint32_t slot_s, uint32_t p_s, uint32_t tmem, Misc& M, int* err) {
+__device__ bool mma_qk(const TileCursor& cur, const MmaState& st, uint32_t q_s, uint32_t slot_s,
+                       uint32_t tmem, Misc& M, int* err) {
   constexpr int NCH = LayoutT<L>::kChunks;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 64, false, false);
+  volatile int* abort_flag = &M.abort;
+  if (cur.t == cur.t_lo && !mbar_wait(&M.q_full, st.seg_count & 1, abort_flag, err)) return false;
+  for (int c = 0; c < NCH; ++c) {
+    if (!mbar_wait(&M.full[c], st.tile_count & 1, abort_flag, err)) return false;
+    DSV4B_TR_ROLE(1, 10, c);
+    tc_fence_after();
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint64_t ad = sdesc_sw128(slot_s + c * kSlotBytes + kk * 32, 16, 1024);
+      const uint64_t bd = sdesc_sw128(q_s + c * kQChunkBytes + kk * 32, 16, 1024);
+      umma_bf16_ss(tmem + kColS, ad, bd, idesc_qk, (c | kk) != 0);
+    }
+  }
+  umma_commit(&M.s_full);
+  DSV4B_TR_ROLE(1, 11, st.tile_count);
+  if (cur.t + 1 == cur.t_hi) umma_commit(&M.q_empty);
+  return true;
+}
+
+// O^T[512 dims, 64 heads] += V^T[dims, 128 tok] . P^T[128 tok, heads], then
+// the row sums; releases the chunk slots M-block by M-block.
+template <int L>
+__device__ bool mma_pv(const TileCursor& cur, const MmaState& st, uint32_t slot_s, uint32_t p_s,
+                       uint32_t tmem, Misc& M, int* err) {
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 64, true, true);
   constexpr uint32_t idesc_sum = idesc_bf16_f32(64, 64, false, true);
   const uint32_t ones_s = smem_u32(&M.stage[0][0]);
-  volatile int* abort_flag = &M.abort;
-
-  TileCursor cur = cursor_begin(p, sm);
-  int tile_count = 0, seg_count = 0;
-  while (cur.valid) {
-    const bool seg_first = cur.t == cur.t_lo;
-    const bool seg_last = cur.t + 1 == cur.t_hi;
-    if (seg_first) {
-      if (!mbar_wait(&M.q_full, seg_count & 1, abort_flag, err)) return;
-      ++seg_count;
-    }
-    // S^T[128 tok, 64 heads] = K_tile[128, d_qk] . Q^T  (K-major A and B)
-    for (int c = 0; c < NCH; ++c) {
-      if (!mbar_wait(&M.full[c], tile_count & 1, abort_flag, err)) return;
-      DSV4B_TR_ROLE(1, 10, c);
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ad = sdesc_sw128(slot_s + c * kSlotBytes + kk * 32, 16, 1024);
-        const uint64_t bd = sdesc_sw128(q_s + c * kQChunkBytes + kk * 32, 16, 1024);
-        umma_bf16_ss(tmem + kColS, ad, bd, idesc_qk, (c | kk) != 0);
-      }
-    }
-    umma_commit(&M.s_full);
-    DSV4B_TR_ROLE(1, 11, tile_count);
-    if (seg_last) umma_commit(&M.q_empty);
-
-    // O^T[512 dims, 64 heads] += V^T[dims, 128 tok] . P^T[128 tok, heads]
-    if (!mbar_wait(&M.p_full, tile_count & 1, abort_flag, err)) return;
-    DSV4B_TR_ROLE(1, 12, tile_count);
-    tc_fence_after();
+  const bool seg_first = cur.t == cur.t_lo;
+  if (!mbar_wait(&M.p_full, st.tile_count & 1, &M.abort, err)) return false;
+  DSV4B_TR_ROLE(1, 12, st.tile_count);
+  tc_fence_after();
 #pragma unroll 1
-    for (int m = 0; m < 4; ++m) {
+  for (int m = 0; m < 4; ++m) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = sdesc_sw128(slot_s + (2 * m) * kSlotBytes + kk * 2048, kSlotBytes, 1024);
-        const uint64_t bd = sdesc_sw128(p_s + kk * 2048, 8192, 1024);
-        umma_bf16_ss(tmem + kColO + 64 * m, ad, bd, idesc_pv, !(seg_first && kk == 0));
-      }
-      umma_commit(&M.empty[m]);
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t ad = sdesc_sw128(slot_s + (2 * m) * kSlotBytes + kk * 2048, kSlotBytes, 1024);
+      const uint64_t bd = sdesc_sw128(p_s + kk * 2048, 8192, 1024);
+      umma_bf16_ss(tmem + kColO + 64 * m, ad, bd, idesc_pv, !(seg_first && kk == 0));
     }
-    // Row sums on the tensor core: L[64 x heads] += ones[64 x 128 tok] .
-    // P^T, so every row of L (TMEM lane 0 included) holds sum_tok P for
-    // each head, summed from the same bf16 P that enters O.
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-      umma_bf16_ss(tmem + kColL, sdesc_sw128(ones_s, 16, 1024), sdesc_sw128(p_s + kk * 2048, 8192, 1024),
-                   idesc_sum, !(seg_first && kk == 0));
-    if (LayoutT<L>::kPInRopeSlot) umma_commit(&M.empty[4]);
-    DSV4B_TR_ROLE(1, 13, tile_count);
-    if (seg_last) umma_commit(&M.o_full);
-    ++tile_count;
-    cur = cursor_next(p, sm, cur);
+    umma_commit(&M.empty[m]);
   }
+  // Row sums on the tensor core: L[64 x heads] += ones[64 x 128 tok] .
+  // P^T, so every row of L (TMEM lane 0 included) holds sum_tok P for
+  // each head, summed from the same bf16 P that enters O.
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_bf16_ss(tmem + kColL, sdesc_sw128(ones_s, 16, 1024), sdesc_sw128(p_s + kk * 2048, 8192, 1024),
+                 idesc_sum, !(seg_first && kk == 0));
+  if (LayoutT<L>::kPInRopeSlot) umma_commit(&M.empty[4]);
+  DSV4B_TR_ROLE(1, 13, st.tile_count);
+  if (cur.t + 1 == cur.t_hi) umma_commit(&M.o_full);
+  return true;
 }
 
 // ------------------------------------------------------------- softmax
@@ -673,9 +644,12 @@ __device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& 
 template <int L>
 __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                             const int32_t* num_splits, float* lse_accum, float* o_accum,
-                            uint32_t p_s, uint32_t tmem, Misc& M, int* err, int cluster_c) {
+                            uint32_t q_s, uint32_t slot_s, uint32_t p_s, uint32_t tmem, Misc& M, int* err,
+                            int cluster_c) {
   const int st = threadIdx.x - kProducerThreads;  // 0..127 = token row = TMEM lane
   const int q = st >> 5;
+  const bool mma_lane = st == 0;  // lane 0 of warp kMmaWarp
+  MmaState ms;
   const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
   const float scale_log2 = p.sm_scale * kLog2e;
   volatile int* abort_flag = &M.abort;
@@ -686,6 +660,13 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
   if (cluster_c > 1 && !cur.valid && st < 64) {  // a cluster rank with no tiles
     M.red[1][st] = -INFINITY;
     M.red[2][st] = 0.0f;
+  }
+  // MMA issue of the first tile; later tiles' QK^T follows the previous PV.
+  if (q == 0) {
+    bool ok = true;
+    if (mma_lane && cur.valid) ok = mma_qk<L>(cur, ms, q_s, slot_s, tmem, M, err);
+    __syncwarp();
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
   }
   while (cur.valid) {
     const bool seg_first = cur.t == cur.t_lo;
@@ -715,6 +696,18 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     tc_fence_before();
     mbar_arrive(&M.p_full);
     if (st == 0) DSV4B_TR_ROLE(2, 23, tile_count);
+    const TileCursor nxt = cursor_next(p, sm, cur);
+    if (q == 0) {  // the MMA issuer's turn: PV of this tile, QK^T of the next
+      bool ok = true;
+      if (mma_lane) {
+        ok = mma_pv<L>(cur, ms, slot_s, p_s, tmem, M, err);
+        if (cur.t + 1 == cur.t_hi) ++ms.seg_count;
+        ++ms.tile_count;
+        if (ok && nxt.valid) ok = mma_qk<L>(nxt, ms, q_s, slot_s, tmem, M, err);
+      }
+      __syncwarp();
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    }
 
     if (seg_last) {
       if (!mbar_wait(&M.o_full, seg_count & 1, abort_flag, err)) return;
@@ -732,7 +725,7 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
       ++seg_count;
     }
     ++tile_count;
-    cur = cursor_next(p, sm, cur);
+    cur = nxt;
   }
 }
 
@@ -900,12 +893,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t slot_s = base_addr + SP::kSlotOff;
   const uint32_t p_s = base_addr + SP::kPOff;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const dsv4b_sched_meta sm = sched[blockIdx.x];
   const int g = blockIdx.y;
 
   if (threadIdx.x == 0) {
-    for (int c = 0; c < 9; ++c) mbar_init(&M.full[c], kProducerThreads);
+    for (int c = 0; c < 9; ++c) mbar_init(&M.full[c], kGroupThreads);  // one producer group per chunk
     for (int e = 0; e < 5; ++e) mbar_init(&M.empty[e], 1);
     mbar_init(&M.s_full, 1);
     mbar_init(&M.p_full, kSoftmaxThreads);
@@ -928,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
     fence_mbarrier_init();
   }
-  if (warp >= kProducerWarps && warp < kMmaWarp) fill_ones(M, threadIdx.x - kProducerThreads);
+  if (warp >= kProducerWarps) fill_ones(M, threadIdx.x - kProducerThreads);
   if (warp == kMmaWarp) {
     tmem_alloc(&M.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -940,10 +933,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kProducerWarps) {
     run_producer<L>(p, sm, g, q_s, slot_s, M, err);
-  } else if (warp < kMmaWarp) {
-    run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, p_s, tmem, M, err, cluster_c);
-  } else if (lane == 0) {
-    run_mma<L>(p, sm, q_s, slot_s, p_s, tmem, M, err);
+  } else {
+    run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, q_s, slot_s, p_s, tmem, M, err, cluster_c);
   }
 
   tc_fence_before();
