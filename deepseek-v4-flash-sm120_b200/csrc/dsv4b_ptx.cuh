@@ -286,6 +286,11 @@ __device__ __forceinline__ void sts_v4(uint32_t saddr, uint4 v) {
 }
 
 // Bulk prefetch of [p, p+bytes) into L2 (p 16-B aligned, bytes % 16 == 0).
+// L2 prefetch of the 128-byte line holding p (a hint: nothing is returned).
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }

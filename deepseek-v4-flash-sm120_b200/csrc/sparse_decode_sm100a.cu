@@ -56,6 +56,19 @@ constexpr int kTraceCtas = 8;
 __device__ unsigned long long g_trace[kTraceCtas * 3 * 128];
 __shared__ unsigned long long* s_trace_base;
 __shared__ int s_trace_n[3];
+// Per-producer-warp log (lane 0 of warps 0-7): 64 words per warp.
+__device__ unsigned long long g_trace_w[kTraceCtas * 8 * 64];
+__shared__ int s_trace_wn[8];
+#define DSV4B_TR_WARP(ev, a)                                                                   \
+  do {                                                                                         \
+    const int w_ = threadIdx.x >> 5;                                                           \
+    if ((threadIdx.x & 31) == 0 && w_ < 8 && blockIdx.x < kTraceCtas && blockIdx.y == 0) {     \
+      const int k_ = s_trace_wn[w_]++;                                                         \
+      if (k_ < 64)                                                                             \
+        g_trace_w[(blockIdx.x * 8 + w_) * 64 + k_] =                                           \
+            ((unsigned long long)clock64() << 24) | ((ev) << 16) | ((unsigned)(a) & 0xFFFFu);  \
+    }                                                                                          \
+  } while (0)
 #define DSV4B_TR_ROLE(role, ev, a)                                                        \
   do {                                                                                    \
     const int k_ = s_trace_n[role]++;                                                     \
@@ -66,6 +79,9 @@ __shared__ int s_trace_n[3];
 #else
 #define DSV4B_TR_ROLE(role, ev, a) \
   do {                             \
+  } while (0)
+#define DSV4B_TR_WARP(ev, a) \
+  do {                       \
   } while (0)
 #endif
 
@@ -153,30 +169,30 @@ __device__ __forceinline__ int empty_of(int c) {
 // columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
 // pair one PV M-block releases.
 //
-// Producer groups.  Group 0 (warps 0-3) fills chunk pairs 0-1 of every
-// tile, group 1 (warps 4-7) pairs 2-3 and the RoPE chunk.  Within a group,
-// warp w owns tile rows 32w..32w+31 and handles four of them per pass: in
-// pass k lane l works on row 32w + 4k + (l >> 3) and on the 16-byte column
-// q = l & 7 of a 128-byte block of that row, so a warp load reads four
-// rows x 128 contiguous bytes (whole 32-byte sectors).  A "chunk pair" is
-// 128 columns = two 64-column SW128 chunk slots = one V32 scale tile = the
-// slot pair one PV M-block releases.
+// Gather mapping.  Producer warp w owns tile rows 16w..16w+15 and handles
+// four of them per pass: in pass k lane l works on row 16w + 4k + (l >> 3)
+// and on the 16-byte column q = l & 7 of a 128-byte block of that row.  A
+// warp load instruction therefore reads four rows x 128 contiguous bytes
+// (whole 32-byte sectors), and the unit of work is a "chunk pair": 128
+// columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
+// pair one PV M-block releases.
 //
-// Random 656-B rows arrive at roughly 21-25 GB/s per SM, so a tile's 84 KB
-// needs a whole tile period in flight.  The hand-off of stored slots (proxy
-// fence + mbarrier arrive) waits for every load the thread has
-// outstanding, so each group issues its share of tile t+1 right after its
-// own last hand-off of tile t: its loads then stream in during the whole
-// period until the group's next fill, and the two groups' loads are
-// staggered.
-constexpr int kGroupThreads = kProducerThreads / 2;  // 128
-constexpr int kRowsPerThread = 8;
+// Loads are split in two register phases per tile.  Phase A (pairs 0-1 and
+// the scales) is issued at the end of the previous tile together with an
+// L2 bulk prefetch of each whole row, and landed there.  Phase B (pairs 2-3
+// and MODEL1 RoPE) is issued after pairs 0-1 are stored and hits L2; the
+// V32 RoPE chunk is loaded after pair 3, while waiting for the previous PV.  A proxy fence
+// followed by an mbarrier arrive waits for all of the thread's outstanding
+// loads, so every hand-off happens with no load in flight.
+constexpr int kRowsPerThread = 4;
 
 template <int L>
-struct GroupRegs {
-  uint4 f[2][kRowsPerThread];  // this group's two chunk pairs (MODEL1 pair 3, q >= 4: RoPE part 0)
-  uint2 sc[kRowsPerThread];    // V32: the pairs' two fp32 scales; MODEL1: the row's 8 UE8M0 bytes
-  uint4 rp[kRowsPerThread];    // group 1: V32 RoPE; MODEL1 RoPE part 1 (q >= 4)
+struct ProdRegs {
+  RowSrc rs[kRowsPerThread];
+  uint4 fa[2][kRowsPerThread];  // phase A: pairs 0, 1
+  uint4 sc[kRowsPerThread];     // V32: 4 fp32 scales; MODEL1: 8 UE8M0 bytes in .x/.y
+  uint4 fb[2][kRowsPerThread];  // phase B: pairs 2, 3 (MODEL1 pair 3: fp8 or RoPE part 0)
+  uint4 rp[kRowsPerThread];     // V32 RoPE; MODEL1 RoPE part 1
 };
 
 // Flat cache index of tile row r, or -1 for padding (>= the row's attended
@@ -191,38 +207,64 @@ __device__ __forceinline__ uint4 ldg_or_zero(bool ok, const uint8_t* ptr) {
   return ok ? ldg_nc_v4(ptr) : make_uint4(0, 0, 0, 0);
 }
 
-// Issues this group's loads of one tile (rows given by their flat indices).
 template <int L>
-__device__ __forceinline__ void group_load(const dsv4b_decode_params& p, const TileCursor& c, int grp,
-                                           int q, const int (&idx)[kRowsPerThread], GroupRegs<L>& R) {
+__device__ __forceinline__ void rows_of(const dsv4b_decode_params& p, const TileCursor& c,
+                                        const int (&idx)[kRowsPerThread], ProdRegs<L>& R) {
   const TileSpan ts = tile_span(p, c);
 #pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k)
+    R.rs[k] = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
+}
+
+template <int L>
+__device__ __forceinline__ void load_phase_a(int q, ProdRegs<L>& R) {
+#pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) {
-    const RowSrc r = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
-    const int c0 = 256 * grp;  // byte offset of this group's first pair
-    R.f[0][k] = ldg_or_zero(r.valid, r.rec + c0 + 16 * q);
+    const RowSrc& r = R.rs[k];
+    R.fa[0][k] = ldg_or_zero(r.valid, r.rec + 16 * q);
+    R.fa[1][k] = ldg_or_zero(r.valid, r.rec + 128 + 16 * q);
+    R.sc[k] = load_scales<L>(r);
+  }
+}
+
+template <int L>
+__device__ __forceinline__ void load_phase_b(int q, ProdRegs<L>& R) {
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    const RowSrc& r = R.rs[k];
+    R.fb[0][k] = ldg_or_zero(r.valid, r.rec + 256 + 16 * q);
     if constexpr (L == DSV4B_LAYOUT_V32) {
-      R.f[1][k] = ldg_or_zero(r.valid, r.rec + c0 + 128 + 16 * q);
-      R.sc[k] = r.valid ? ldg_nc_v2(r.scl + 8 * grp) : make_uint2(0, 0);
-      if (grp == 1) R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 16 * q);
-    } else {
-      if (grp == 0 || q < 4) {
-        R.f[1][k] = ldg_or_zero(r.valid, r.rec + c0 + 128 + 16 * q);
-      } else {  // MODEL1 pair 3, lanes 4-7: the 64 bf16 RoPE columns
-        R.f[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
-        R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
-      }
-      R.sc[k] = r.valid ? ldg_nc_v2(r.scl) : make_uint2(0, 0);
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
+    } else if (q < 4) {  // MODEL1 pair 3: fp8 columns 384..447 ...
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
+    } else {             // ... and the 64 bf16 RoPE columns
+      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
+      R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
     }
   }
 }
 
-// Scale of the 16 columns lane q holds in chunk pair m (j = m & 1 within
-// the group).
+// Folds registers into one word stored to shared memory: pins the loads
+// (and their completion) to this point, so the code generator cannot sink
+// them into the chunk loop where the latency would be exposed per chunk.
 template <int L>
-__device__ __forceinline__ float pair_scale(const uint2& sc, int m, int q) {
+__device__ __forceinline__ void land_phase_a(const ProdRegs<L>& R, const int (&idx)[kRowsPerThread],
+                                             Misc& M) {
+  uint32_t x = 0;
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) {
+    x ^= R.fa[0][k].x ^ R.fa[0][k].y ^ R.fa[0][k].z ^ R.fa[0][k].w;
+    x ^= R.fa[1][k].x ^ R.fa[1][k].y ^ R.fa[1][k].z ^ R.fa[1][k].w;
+    x ^= R.sc[k].x ^ R.sc[k].y ^ R.sc[k].z ^ R.sc[k].w ^ (uint32_t)idx[k];
+  }
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(&M.sink_word)), "r"(x) : "memory");
+}
+
+// Scale of the 16 columns lane q holds in chunk pair m.
+template <int L>
+__device__ __forceinline__ float pair_scale(const uint4& sc, int m, int q) {
   if constexpr (L == DSV4B_LAYOUT_V32) {
-    return __uint_as_float((m & 1) ? sc.y : sc.x);
+    return __uint_as_float(m == 0 ? sc.x : m == 1 ? sc.y : m == 2 ? sc.z : sc.w);
   } else {
     const int byte = 2 * m + (q >> 2);  // 64-column UE8M0 tiles
     const uint32_t w = byte < 4 ? sc.x : sc.y;
@@ -248,18 +290,15 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   using LT = LayoutT<L>;
   constexpr int NCH = LT::kChunks;
   const int ptid = threadIdx.x;
-  const int grp = ptid / kGroupThreads;
-  const int gt = ptid - grp * kGroupThreads;
-  const int w = gt >> 5, lane = gt & 31;
+  const int w = ptid >> 5, lane = ptid & 31;
   const int q = lane & 7;
-  const int row0 = 32 * w + (lane >> 3);  // row of pass k: row0 + 4k
+  const int row0 = 16 * w + (lane >> 3);  // row of pass k: row0 + 4k
 
   TileCursor cur = cursor_begin(p, sm);
   if (!cur.valid) return;
   TileCursor nxt = cursor_next(p, sm, cur);
 
-  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks
-  // (all 256 producer threads).
+  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks.
   auto issue_q = [&](const TileCursor& c) {
     const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
                               (int64_t)c.ri.b * p.stride_q_b + (int64_t)c.ri.s * p.stride_q_s;
@@ -276,13 +315,16 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   // The first row's Q^T is in flight together with the first tile's loads.
   issue_q(cur);
 
-  GroupRegs<L> R;
+  ProdRegs<L> R;
   int idx[kRowsPerThread];
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
-  group_load<L>(p, cur, grp, q, idx, R);
+  rows_of<L>(p, cur, idx, R);
+  load_phase_a<L>(q, R);
+  load_phase_b<L>(q, R);
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nxt.valid ? producer_index(p, nxt, row0 + 4 * k) : -1;
+  land_phase_a<L>(R, idx, M);
 
   int tile_count = 0, seg_count = 0;
   volatile int* abort_flag = &M.abort;
@@ -302,45 +344,64 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     if (ptid == 0) DSV4B_TR_ROLE(0, 1, tile_count);
     const uint32_t wait_par = (tile_count - 1) & 1;
 
+    // pairs 0, 1 (phase A registers)
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int m = 2 * grp + j;
+    for (int m = 0; m < 2; ++m) {
+      if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k)
+        store_pair_fp8(slot_s, m, row0 + 4 * k, q, R.fa[m][k], pair_scale<L>(R.sc[k], m, q));
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[2 * m]);
+      mbar_arrive(&M.full[2 * m + 1]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+    }
+    if constexpr (LayoutT<L>::kPInRopeSlot) {
+      // V32 RoPE chunk: issued here so it lands while pairs 2, 3 are stored.
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k)
+        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
+    }
+    // pairs 2, 3 (phase B registers)
+#pragma unroll
+    for (int m = 2; m < 4; ++m) {
       if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) {
         const int row = row0 + 4 * k;
         if (L == DSV4B_LAYOUT_MODEL1 && m == 3 && q >= 4) {
           const uint32_t slot = slot_s + 7 * kSlotBytes;  // MODEL1 RoPE chunk
-          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.f[1][k]);
+          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.fb[1][k]);
           sts_v4(slot + sw128_off(row, 2 * (q - 4) + 1), R.rp[k]);
         } else {
-          store_pair_fp8(slot_s, m, row, q, R.f[j][k], pair_scale<L>(R.sc[k], m, q));
+          store_pair_fp8(slot_s, m, row, q, R.fb[m - 2][k], pair_scale<L>(R.sc[k], m, q));
         }
       }
       fence_proxy_async_smem();
       mbar_arrive(&M.full[2 * m]);
       mbar_arrive(&M.full[2 * m + 1]);
-      if (gt == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
     }
     if constexpr (LayoutT<L>::kPInRopeSlot) {
-      if (grp == 1) {
-        // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
-        if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
-        const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
+      // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
+      if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
+      const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
 #pragma unroll
-        for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
-        fence_proxy_async_smem();
-        mbar_arrive(&M.full[NCH - 1]);
-        if (gt == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
-      }
+      for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[NCH - 1]);
+      if (ptid == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
     }
 
-    // This group's loads of the next tile, then the indices of the one after.
+    // batch: phase A of the next tile, indices of the one after
     const TileCursor nn = cursor_next(p, sm, nxt);
     if (nxt.valid) {
-      group_load<L>(p, nxt, grp, q, idx, R);
+      rows_of<L>(p, nxt, idx, R);
+      load_phase_a<L>(q, R);
+      load_phase_b<L>(q, R);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
+      land_phase_a<L>(R, idx, M);
     }
     if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
@@ -898,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int g = blockIdx.y;
 
   if (threadIdx.x == 0) {
-    for (int c = 0; c < 9; ++c) mbar_init(&M.full[c], kGroupThreads);  // one producer group per chunk
+    for (int c = 0; c < 9; ++c) mbar_init(&M.full[c], kProducerThreads);
     for (int e = 0; e < 5; ++e) mbar_init(&M.empty[e], 1);
     mbar_init(&M.s_full, 1);
     mbar_init(&M.p_full, kSoftmaxThreads);
@@ -908,6 +969,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     M.abort = 0;
 #ifdef DSV4B_TRACE
     s_trace_n[0] = s_trace_n[1] = s_trace_n[2] = 0;
+    for (int i = 0; i < 8; ++i) s_trace_wn[i] = 0;
     s_trace_base = (blockIdx.x < kTraceCtas && blockIdx.y == 0) ? g_trace + blockIdx.x * 3 * 128 : nullptr;
     if (s_trace_base) {
       for (int i = 0; i < 3 * 128; ++i) s_trace_base[i] = 0;
@@ -1060,6 +1122,12 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
 }
 
 #ifdef DSV4B_TRACE
+extern "C" DSV4B_API int dsv4b_debug_trace_read_warps(unsigned long long* dst, int max_words) {
+  const int n = kTraceCtas * 8 * 64 < max_words ? kTraceCtas * 8 * 64 : max_words;
+  cudaMemcpyFromSymbol(dst, g_trace_w, n * sizeof(unsigned long long));
+  return n;
+}
+
 extern "C" DSV4B_API int dsv4b_debug_trace_read(unsigned long long* dst, int max_words) {
   const int n = kTraceCtas * 3 * 128 < max_words ? kTraceCtas * 3 * 128 : max_words;
   cudaMemcpyFromSymbol(dst, g_trace, n * sizeof(unsigned long long));
