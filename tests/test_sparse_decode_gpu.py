@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from dsv4b_testutil import assert_matches, oracle_for
+from dsv4b_testutil import LSE_ATOL, LSE_RTOL, OUT_ATOL, OUT_RTOL, assert_matches, oracle_for
 from golden_io import golden_names, load_golden
 from oracle import schedule_oracle as SO
 from oracle import sparse_decode_oracle as O
@@ -307,3 +307,31 @@ def test_patch_wrapper_routes_sparse_to_b200():
     assert fake.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, meta, is_fp8_kvcache=False,
                                        indices=None) == "upstream"
     assert len(calls) == 1
+
+
+@pytest.mark.parametrize("mode", ["batch", "head"])
+def test_partition_shards_match_full_decode(mode):
+    """The multi-GPU partition decodes each shard independently (no data-path
+    collective); on one GPU the reassembled shards equal the full decode."""
+    from deepseek_v4_kernel import partition
+    spec = _kc().BatchSpec(b=6, s_q=1, h_q=128, topk=640, ctx=4096, page_block=64, seed=23)
+    bt = _kc().make_batch(spec)
+    full_out, full_lse, _, _ = _run(bt)
+    world = 2
+    outs = []
+    for rank in range(world):
+        if mode == "batch":
+            q, idx, _, (lo, hi) = partition.shard_batch(bt.q, bt.indices, None, rank, world)
+            shard = _kc().Batch(q=q, kv=bt.kv, indices=idx, attn_sink=bt.attn_sink, sm_scale=bt.sm_scale,
+                                spec=spec)
+        else:
+            q, sink, (lo, hi) = partition.shard_heads(bt.q, bt.attn_sink, rank, world)
+            shard = _kc().Batch(q=q, kv=bt.kv, indices=bt.indices, attn_sink=sink, sm_scale=bt.sm_scale,
+                                spec=spec)
+        o, l, _, _ = _run(shard)
+        outs.append((o, l))
+    # shards get their own split plans, so only the accumulation order differs
+    got = torch.cat([o for o, _ in outs], dim=0 if mode == "batch" else 2)
+    got_lse = torch.cat([l for _, l in outs], dim=0 if mode == "batch" else 1)
+    torch.testing.assert_close(got.float(), full_out.float(), atol=OUT_ATOL, rtol=OUT_RTOL)
+    torch.testing.assert_close(got_lse, full_lse, atol=LSE_ATOL, rtol=LSE_RTOL)
