@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 4])
     ap.add_argument("--mode", choices=["batch", "head"], default="batch")
     ap.add_argument("--batch", type=int, default=None, help="override b (per rank)")
+    ap.add_argument("--ctx", type=int, default=None,
+                    help="override the per-request context (cache size); same per-step work "
+                         "(b, h_q, top-k) on a smaller cache, for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
@@ -127,12 +130,14 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def workload(cfg: int, batch_override, rank: int):
+def workload(cfg: int, batch_override, rank: int, ctx_override=None):
     from deepseek_v4_kernel import kvcache
     spec = kvcache.CONFIGS[cfg]
     spec = kvcache.BatchSpec(**{**spec.__dict__, "seed": 1000 + rank})
     if batch_override:
         spec.b = batch_override
+    if ctx_override:
+        spec.ctx, spec.cache_ctx = ctx_override, None
     return spec
 
 
@@ -147,7 +152,7 @@ def algorithmic(spec, h_q_local=None):
 
 
 def workload_name(spec, mode, world):
-    return (f"config{'' if spec is None else ''}: b{spec.b} s_q{spec.s_q} h_q{spec.h_q} "
+    return (f"b{spec.b} s_q{spec.s_q} h_q{spec.h_q} "
             f"topk{spec.topk} ctx{spec.ctx} page{spec.page_block} {spec.layout.upper()} fp8 KV"
             + (f", {mode}-sharded x{world}" if world > 1 else ""))
 
@@ -200,7 +205,7 @@ def run_reference(args, spec, world, rank):
         "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_name(spec, args.mode, 1), "cpu_threads": threads},
+        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, 1), "cpu_threads": threads},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
@@ -427,7 +432,7 @@ def run_ours(args, spec, world, rank, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q / latent / RoPE, random page tables, distinct top-k)",
-        "config": {"workload": f"config{args.config} " + workload_name(spec, args.mode, world),
+        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, world),
                    "l2": "flushed before every step (256 MiB write)",
                    "parallelism": f"{args.mode}-shard x{world}" if world > 1 else "single GPU",
                    "num_sm_parts": parts, "cluster_size": cluster},
@@ -456,7 +461,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    spec = workload(args.config, args.batch, rank if args.mode == "batch" else 0)
+    spec = workload(args.config, args.batch, rank if args.mode == "batch" else 0, args.ctx)
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, spec, world, rank)
