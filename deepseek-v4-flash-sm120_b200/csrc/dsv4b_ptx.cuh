@@ -212,6 +212,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "r"(taddr));
 }
 
+// 64 consecutive columns (two x32 loads; one tc_wait_ld covers both).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
+  tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
   asm volatile(

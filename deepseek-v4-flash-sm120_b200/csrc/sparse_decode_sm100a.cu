@@ -273,15 +273,18 @@ __device__ __forceinline__ float pair_scale(const uint4& sc, int m, int q) {
 }
 
 // Dequantises lane q's 16 e4m3 of chunk pair m of one row into its two
-// 16-byte units of chunk slot 2m + q/4.
+// 16-byte units of chunk slot 2m + q/4.  Lanes 4-7 (the second slot) store
+// their high unit first, so each store instruction covers all eight
+// 16-byte granules of a row (no bank conflict between the two slots).
 __device__ __forceinline__ void store_pair_fp8(uint32_t slot_s, int m, int row, int q, uint4 v,
                                                float s) {
   uint4 lo, hi;
   dq16(v, s, lo, hi);
   const uint32_t slot = slot_s + (2 * m + (q >> 2)) * kSlotBytes;
   const int u = 2 * (q & 3);
-  sts_v4(slot + sw128_off(row, u), lo);
-  sts_v4(slot + sw128_off(row, u + 1), hi);
+  const bool swap = (q & 4) != 0;
+  sts_v4(slot + sw128_off(row, u + (swap ? 1 : 0)), swap ? hi : lo);
+  sts_v4(slot + sw128_off(row, u + (swap ? 0 : 1)), swap ? lo : hi);
 }
 
 template <int L>
@@ -347,13 +350,17 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     // pairs 0, 1 (phase A registers)
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
+      DSV4B_TR_WARP(55, m);
       if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
+      DSV4B_TR_WARP(51, m);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k)
         store_pair_fp8(slot_s, m, row0 + 4 * k, q, R.fa[m][k], pair_scale<L>(R.sc[k], m, q));
+      DSV4B_TR_WARP(56, m);
       fence_proxy_async_smem();
       mbar_arrive(&M.full[2 * m]);
       mbar_arrive(&M.full[2 * m + 1]);
+      DSV4B_TR_WARP(52, m);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
     }
     if constexpr (LayoutT<L>::kPInRopeSlot) {
@@ -365,7 +372,9 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     // pairs 2, 3 (phase B registers)
 #pragma unroll
     for (int m = 2; m < 4; ++m) {
+      DSV4B_TR_WARP(55, m);
       if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
+      DSV4B_TR_WARP(51, m);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) {
         const int row = row0 + 4 * k;
@@ -377,31 +386,40 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
           store_pair_fp8(slot_s, m, row, q, R.fb[m - 2][k], pair_scale<L>(R.sc[k], m, q));
         }
       }
+      DSV4B_TR_WARP(56, m);
       fence_proxy_async_smem();
       mbar_arrive(&M.full[2 * m]);
       mbar_arrive(&M.full[2 * m + 1]);
+      DSV4B_TR_WARP(52, m);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
     }
     if constexpr (LayoutT<L>::kPInRopeSlot) {
       // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
+      DSV4B_TR_WARP(55, 4);
       if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
+      DSV4B_TR_WARP(51, 4);
       const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), R.rp[k]);
+      DSV4B_TR_WARP(56, 4);
       fence_proxy_async_smem();
       mbar_arrive(&M.full[NCH - 1]);
+      DSV4B_TR_WARP(52, 4);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
     }
 
-    // batch: phase A of the next tile, indices of the one after
+    // The next tile's loads, then the indices of the tile after it.
     const TileCursor nn = cursor_next(p, sm, nxt);
     if (nxt.valid) {
+      DSV4B_TR_WARP(57, tile_count);
       rows_of<L>(p, nxt, idx, R);
       load_phase_a<L>(q, R);
       load_phase_b<L>(q, R);
+      DSV4B_TR_WARP(50, tile_count);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
       land_phase_a<L>(R, idx, M);
+      DSV4B_TR_WARP(58, tile_count);
     }
     if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
@@ -504,15 +522,12 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
   // Row sums: the row-sum UMMA left sum_tok P of head j in column kColL + j
   // of every row; warp 0 reads TMEM lane 0.
   if (q == 0) {
+    float lv[64];
+    tmem_ld64(tl + kColL, lv);
+    tc_wait_ld();
+    if (lane == 0) {
 #pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float lv[16];
-      tmem_ld16(tl + kColL + 16 * c16, lv);
-      tc_wait_ld();
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) M.red[0][16 * c16 + j] = lv[j];
-      }
+      for (int j = 0; j < 64; ++j) M.red[0][j] = lv[j];
     }
   }
   named_bar_sync(1, kSoftmaxThreads);
@@ -545,15 +560,11 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
 #pragma unroll 1
     for (int mh = 0; mh < 8; ++mh) {  // 4 M-blocks x 2 head halves
       const int m = mh >> 1, hf = mh & 1;
+      float ov[32];
+      tmem_ld32(tl + kColO + 64 * m + 32 * hf, ov);
+      tc_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float ov[16];
-        tmem_ld16(tl + kColO + 64 * m + 32 * hf + 16 * c, ov);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          M.stage[16 * c + j][st] = __float2bfloat16_rn(ov[j] * M.scale_o[32 * hf + 16 * c + j]);
-      }
+      for (int j = 0; j < 32; ++j) M.stage[j][st] = __float2bfloat16_rn(ov[j] * M.scale_o[32 * hf + j]);
       named_bar_sync(1, kSoftmaxThreads);
       const int head = g * kHeadsPerCta + 32 * hf + r;
       if (head < p.h_q) {
@@ -570,22 +581,24 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
     float* stage = reinterpret_cast<float*>(&M.stage[0][0]);  // [16][128] fp32
     const int r = st >> 3, part = st & 7;
 #pragma unroll 1
-    for (int mg = 0; mg < 16; ++mg) {  // 4 M-blocks x 4 groups of 16 heads
-      const int m = mg >> 2, hg = mg & 3;
-      float ov[16];
-      tmem_ld16(tl + kColO + 64 * m + 16 * hg, ov);
+    for (int m = 0; m < 4; ++m) {  // 4 M-blocks, each in 4 rounds of 16 heads
+      float ov[64];
+      tmem_ld64(tl + kColO + 64 * m, ov);
       tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) stage[j * 128 + st] = ov[j] * M.scale_o[16 * hg + j];
-      named_bar_sync(1, kSoftmaxThreads);
-      const int head = g * kHeadsPerCta + 16 * hg + r;
-      if (head < p.h_q) {
-        float4* dst = reinterpret_cast<float4*>(o_accum + ((int64_t)split * p.h_q + head) * kDv + 128 * m);
-        const float4* src = reinterpret_cast<const float4*>(stage + r * 128);
+      for (int hg = 0; hg < 4; ++hg) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[8 * k + part] = src[8 * k + part];
+        for (int j = 0; j < 16; ++j) stage[j * 128 + st] = ov[16 * hg + j] * M.scale_o[16 * hg + j];
+        named_bar_sync(1, kSoftmaxThreads);
+        const int head = g * kHeadsPerCta + 16 * hg + r;
+        if (head < p.h_q) {
+          float4* dst = reinterpret_cast<float4*>(o_accum + ((int64_t)split * p.h_q + head) * kDv + 128 * m);
+          const float4* src = reinterpret_cast<const float4*>(stage + r * 128);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) dst[8 * k + part] = src[8 * k + part];
+        }
+        named_bar_sync(1, kSoftmaxThreads);
       }
-      named_bar_sync(1, kSoftmaxThreads);
     }
   }
 }
@@ -608,15 +621,14 @@ __device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, b
                                                  float& m_run, Misc& M) {
   const int st = threadIdx.x - kProducerThreads;
   const int q = st >> 5, lane = st & 31;
-#pragma unroll
-  for (int c16 = 0; c16 < 4; ++c16) {
-    float sv[16];
-    tmem_ld16(tl + kColS + 16 * c16, sv);
+  {
+    float sv[64];
+    tmem_ld64(tl + kColS, sv);
     tc_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 64; ++j) {
       const float mx = warp_max_f32(row_scale != 0.0f ? sv[j] * row_scale : -INFINITY);
-      if (lane == 0) M.red[q][16 * c16 + j] = mx;
+      if (lane == 0) M.red[q][j] = mx;
     }
   }
   named_bar_sync(1, kSoftmaxThreads);
@@ -638,16 +650,17 @@ __device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, b
   }
   const bool any_resc = named_bar_or(1, kSoftmaxThreads, resc);
   if (any_resc && !seg_first) {
-    // 16 O column groups (4 M-blocks x 64 heads) + 4 row-sum groups.
+    // 4 O M-blocks (64 head columns each) + the row sums.
 #pragma unroll 1
-    for (int cc = 0; cc < 20; ++cc) {
-      const uint32_t col = cc < 16 ? kColO + 64 * (cc >> 2) + 16 * (cc & 3) : kColL + 16 * (cc - 16);
-      float ov[16];
-      tmem_ld16(tl + col, ov);
+    for (int cc = 0; cc < 5; ++cc) {
+      const uint32_t col = cc < 4 ? kColO + 64 * cc : kColL;
+      float ov[64];
+      tmem_ld64(tl + col, ov);
       tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) ov[j] *= M.alpha[16 * (cc & 3) + j];
-      tmem_st16(tl + col, ov);
+      for (int j = 0; j < 64; ++j) ov[j] *= M.alpha[j];
+      tmem_st32(tl + col, *reinterpret_cast<float(*)[32]>(&ov[0]));
+      tmem_st32(tl + col + 32, *reinterpret_cast<float(*)[32]>(&ov[32]));
     }
   }
 }
@@ -659,11 +672,12 @@ __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uin
                                                const Misc& M) {
   const int st = threadIdx.x - kProducerThreads;
   bool exceed = false;
+  float sa[64];
+  tmem_ld64(tl + kColS, sa);
+  tc_wait_ld();
 #pragma unroll
   for (int c16 = 0; c16 < 4; ++c16) {
-    float sv[16];
-    tmem_ld16(tl + kColS + 16 * c16, sv);
-    tc_wait_ld();
+    const float* sv = sa + 16 * c16;
     uint32_t pk[8];
 #pragma unroll
     for (int j4 = 0; j4 < 4; ++j4) {
@@ -688,15 +702,12 @@ __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uin
 __device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& M) {
   const int st = threadIdx.x - kProducerThreads;
   if ((st >> 5) == 0) {
+    float lv[64];
+    tmem_ld64(tl + kColL, lv);
+    tc_wait_ld();
+    if (st == 0) {
 #pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float lv[16];
-      tmem_ld16(tl + kColL + 16 * c16, lv);
-      tc_wait_ld();
-      if (st == 0) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) M.red[2][16 * c16 + j] = lv[j];
-      }
+      for (int j = 0; j < 64; ++j) M.red[2][j] = lv[j];
     }
   }
   if (st < 64) M.red[1][st] = m_run;
@@ -862,18 +873,15 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
         const int d = 128 * m + st;
         const int owner = d / D, dl = d - owner * D;
         const uint32_t dst = dsmem_addr(recv_s + self * blk_bytes + (uint32_t)dl * 16u, owner);
+        float ov[64];
+        tmem_ld64(tl + kColO + 64 * m, ov);
+        tc_wait_ld();
+        if (owner != (int)self) {
 #pragma unroll
-        for (int hg = 0; hg < 4; ++hg) {
-          float ov[16];
-          tmem_ld16(tl + kColO + 64 * m + 16 * hg, ov);
-          tc_wait_ld();
-          if (owner != (int)self) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float4 w4 = *reinterpret_cast<const float4*>(&M.scale_o[16 * hg + 4 * k]);
-              dsmem_st_v4(dst + (uint32_t)(4 * hg + k) * (uint32_t)D * 16u, ov[4 * k] * w4.x, ov[4 * k + 1] * w4.y, ov[4 * k + 2] * w4.z,
-                          ov[4 * k + 3] * w4.w);
-            }
+          for (int u = 0; u < 16; ++u) {
+            const float4 w4 = *reinterpret_cast<const float4*>(&M.scale_o[4 * u]);
+            dsmem_st_v4(dst + (uint32_t)u * (uint32_t)D * 16u, ov[4 * u] * w4.x, ov[4 * u + 1] * w4.y,
+                        ov[4 * u + 2] * w4.z, ov[4 * u + 3] * w4.w);
           }
         }
       }
@@ -896,11 +904,12 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
 #pragma unroll 1
     for (int hf = 0; hf < 2; ++hf) {
       if (mine) {
+        float acc32[32];
+        tmem_ld32(tl + kColO + 64 * m + 32 * hf, acc32);
+        tc_wait_ld();
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          float acc[16];
-          tmem_ld16(tl + kColO + 64 * m + 32 * hf + 16 * c, acc);
-          tc_wait_ld();
+          float* acc = acc32 + 16 * c;
           const bool own = (live >> self) & 1u;
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[j] = own ? acc[j] * M.scale_o[32 * hf + 16 * c + j] : 0.0f;
