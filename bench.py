@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 4])
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
+                    help="BASELINE config; 3 = the CUDA-graph batch x context sweep")
     ap.add_argument("--mode", choices=["batch", "head"], default="batch")
     ap.add_argument("--batch", type=int, default=None, help="override b (per rank)")
     ap.add_argument("--ctx", type=int, default=None,
@@ -132,7 +133,7 @@ class ClockSampler:
 # ------------------------------------------------------------------ workload
 def workload(cfg: int, batch_override, rank: int, ctx_override=None):
     from deepseek_v4_kernel import kvcache
-    spec = kvcache.CONFIGS[cfg]
+    spec = kvcache.sweep_spec(32, 131072) if cfg == 3 else kvcache.CONFIGS[cfg]
     spec = kvcache.BatchSpec(**{**spec.__dict__, "seed": 1000 + rank})
     if batch_override:
         spec.b = batch_override
@@ -296,16 +297,12 @@ def run_ours(args, spec, world, rank, local_rank):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
 
     def step(evs=None):
-        if cluster > 1:  # one launch: the clusters merge split rows themselves
-            rc = lib.dsv4b_sparse_decode(pp, tsm.data_ptr(), ns.data_ptr(), parts, ws.data_ptr(), ws.numel(), sh)
-            if evs is not None:
-                evs[1].record(stream)
-        else:
-            rc = lib.dsv4b_sparse_decode_partial(pp, tsm.data_ptr(), ns.data_ptr(), parts, ws.data_ptr(),
-                                                 ws.numel(), sh)
-            if evs is not None:
-                evs[1].record(stream)
-            rc |= lib.dsv4b_combine(pp, ns.data_ptr(), parts, ws.data_ptr(), ws.numel(), sh)
+        # The public entry point: the decode kernel, plus (when the plan
+        # splits rows outside clusters) the combine launched as its
+        # programmatic dependent -- nothing may be enqueued between them.
+        rc = lib.dsv4b_sparse_decode(pp, tsm.data_ptr(), ns.data_ptr(), parts, ws.data_ptr(), ws.numel(), sh)
+        if evs is not None:
+            evs[1].record(stream)
         if rc:
             raise RuntimeError(f"decode failed: {rc}")
 
@@ -330,8 +327,7 @@ def run_ours(args, spec, world, rank, local_rank):
         dist.barrier()
     clocks = sampler.stop()
     dec_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    # with clusters the step is the single decode launch (evs[1] follows it directly)
-    step_ms = dec_ms if cluster > 1 else [e[0].elapsed_time(e[2]) for e in evs]
+    step_ms = dec_ms  # evs[1] follows the step's last launch directly
     t_step = statistics.median(step_ms)
     t_dec = statistics.median(dec_ms)
     assert dk.read_kernel_status(device) == 0, "kernel wait timeout"
@@ -437,7 +433,7 @@ def run_ours(args, spec, world, rank, local_rank):
                    "parallelism": f"{args.mode}-shard x{world}" if world > 1 else "single GPU",
                    "num_sm_parts": parts, "cluster_size": cluster},
         "decode_kernel_us": round(t_dec * 1e3, 2),
-        "combine_us": round((t_step - t_dec) * 1e3, 2),
+        "combine_launched": launches_per_step > 1,
         "sched_meta_us": round(sched_us, 2),
         "roofline_time_us": round(t_roof_us, 2),
         "step_roofline_frac": round(t_roof_us / (t_step * 1e3), 4),
@@ -456,8 +452,80 @@ def run_ours(args, spec, world, rank, local_rank):
             f.write(json.dumps(line) + "\n")
 
 
+def run_sweep(args):
+    """b in {1..32} x context in {8K..300K}, h_q 64, top-k
+    2048; the whole step (flash_mla_with_kvcache with a reused
+    FlashMLASchedMeta) captured in one CUDA graph and replayed, L2 flushed
+    before every replay.  Prints one JSON line whose value is the b 32 /
+    128K point and whose "sweep" lists every point."""
+    import torch
+
+    import deepseek_v4_kernel as dk
+    from deepseek_v4_kernel import kvcache, ops
+
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    points = []
+    for ctx in (8192, 32768, 131072, 300000):
+        for b in (1, 2, 4, 8, 16, 32):
+            spec = kvcache.sweep_spec(b, ctx)
+            bt = kvcache.make_batch(spec, device=device)
+            sched, _ = dk.get_mla_metadata()
+
+            def step():
+                return dk.flash_mla_with_kvcache(bt.q, bt.kv, None, None, 512, sched, softmax_scale=bt.sm_scale,
+                                                 is_fp8_kvcache=True, indices=bt.indices, attn_sink=bt.attn_sink)
+
+            step()
+            torch.cuda.synchronize()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                step()
+            torch.cuda.current_stream().wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            for _ in range(args.warmup):
+                flush.zero_()
+                g.replay()
+            ts = []
+            for _ in range(args.steps):
+                flush.zero_()
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                g.replay()
+                e.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(e) * 1e3)
+            o_ = torch.empty(b, 1, 64, 512, dtype=torch.bfloat16, device=device)
+            l_ = torch.empty(b, 64, 1, dtype=torch.float32, device=device)
+            p = ops.build_params(bt.q, bt.kv, bt.indices, None, bt.attn_sink, None, None, None, 512, bt.sm_scale,
+                                 o_, l_)
+            points.append({"b": b, "ctx": ctx, "us_per_step": round(statistics.median(ts), 2),
+                           "cluster_size": ops.plan_cluster_size(p, ops.num_sm_parts(device, 64))})
+            del g, bt
+            torch.cuda.empty_cache()
+    head = next(pt for pt in points if pt["b"] == 32 and pt["ctx"] == 131072)
+    assert dk.read_kernel_status(device) == 0, "kernel wait timeout"
+    line = {
+        "metric": "sparse_decode_us_per_step", "value": head["us_per_step"], "unit": "us/step", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head["us_per_step"] / 1e3, 5),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q / latent / RoPE, random page tables, distinct top-k)",
+        "config": {"workload": "config3: CUDA-graph sweep, h_q 64, top-k 2048, V32 fp8 KV; value = b32 ctx131072",
+                   "l2": "flushed before every replay (256 MiB write)", "parallelism": "single GPU"},
+        "sweep": points,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.config == 3 and args.impl == "ours":
+        run_sweep(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -242,44 +242,58 @@ __global__ void __launch_bounds__(kSchedThreads)
 // The decode kernel leaves split partials o_accum[split][h_q][512] (already
 // divided by the split's own row sum) and lse_accum[split][h_q].
 constexpr int kCombineThreads = kDv / 4;  // 128
+constexpr int kCombineMaxSplits = 32;       // splits held in registers; more loop
 
+// Launched (outside CUDA-graph capture) as a programmatic dependent of the
+// decode kernel: the CTAs start while the decode grid drains and wait here
+// for its completion (and the visibility of its partials) instead of paying
+// a full launch gap.
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const dsv4b_decode_params p, const int32_t* __restrict__ num_splits,
                    const float* __restrict__ lse_accum, const float* __restrict__ o_accum) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x, head = blockIdx.y, t = threadIdx.x;
   const int s0 = __ldg(num_splits + r), s1 = __ldg(num_splits + r + 1);
   const int n = s1 - s0;
   if (n <= 1) return;  // written by the decode kernel
+  constexpr float kLog2e = 1.4426950408889634f;
   const float* lse_col = lse_accum + (int64_t)s0 * p.h_q + head;
-  float mx = -INFINITY;
-  for (int i = 0; i < n; ++i) mx = fmaxf(mx, __ldg(lse_col + (int64_t)i * p.h_q));
-  float sum = 0.0f;
-  for (int i = 0; i < n; ++i) sum += expf(__ldg(lse_col + (int64_t)i * p.h_q) - mx);
-  const float lse = mx + logf(sum);
-
   const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)s0 * p.h_q + head) * kDv) + t;
   const int64_t step = (int64_t)p.h_q * (kDv / 4);  // float4s between splits
+
+  // Split LSEs (log2 units) and partial rows, all loads issued up front.
+  float l2[kCombineMaxSplits];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kCombineMaxSplits; ++i) {
+    l2[i] = i < n ? __ldg(lse_col + (int64_t)i * p.h_q) * kLog2e : -INFINITY;
+    mx = fmaxf(mx, l2[i]);
+  }
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kCombineMaxSplits; ++i) {
+    l2[i] = i < n ? exp2f(l2[i] - mx) : 0.0f;
+    sum += l2[i];
+  }
+  for (int i = kCombineMaxSplits; i < n; ++i) sum += exp2f(__ldg(lse_col + (int64_t)i * p.h_q) * kLog2e - mx);
+  const float inv = 1.0f / sum;
+  const float lse = (mx + log2f(sum)) / kLog2e;
+
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  int i = 0;
-  for (; i + 4 <= n; i += 4) {
-    float4 v[4];
-    float w[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[k] = __ldg(src + (i + k) * step);
-      w[k] = expf(__ldg(lse_col + (int64_t)(i + k) * p.h_q) - lse);
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      acc.x = fmaf(w[k], v[k].x, acc.x);
-      acc.y = fmaf(w[k], v[k].y, acc.y);
-      acc.z = fmaf(w[k], v[k].z, acc.z);
-      acc.w = fmaf(w[k], v[k].w, acc.w);
+  for (int i = 0; i < kCombineMaxSplits; ++i) {
+    if (i < n) {
+      const float4 v = __ldg(src + i * step);
+      const float wi = l2[i] * inv;
+      acc.x = fmaf(wi, v.x, acc.x);
+      acc.y = fmaf(wi, v.y, acc.y);
+      acc.z = fmaf(wi, v.z, acc.z);
+      acc.w = fmaf(wi, v.w, acc.w);
     }
   }
-  for (; i < n; ++i) {
+  for (int i = kCombineMaxSplits; i < n; ++i) {
     const float4 v = __ldg(src + i * step);
-    const float wi = expf(__ldg(lse_col + (int64_t)i * p.h_q) - lse);
+    const float wi = exp2f(__ldg(lse_col + (int64_t)i * p.h_q) * kLog2e - mx) * inv;
     acc.x = fmaf(wi, v.x, acc.x);
     acc.y = fmaf(wi, v.y, acc.y);
     acc.z = fmaf(wi, v.z, acc.z);
@@ -360,9 +374,24 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
 
 cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
                            const float* lse_accum, const float* o_accum, cudaStream_t stream) {
-  const dim3 grid(p.b * p.s_q, p.h_q);
-  combine_kernel<<<grid, kCombineThreads, 0, stream>>>(p, num_splits, lse_accum, o_accum);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.b * p.s_q, p.h_q, 1);
+  cfg.blockDim = dim3(kCombineThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  // Stream launches: a programmatic dependent of the decode kernel, so its
+  // launch overlaps the decode's tail.  Inside a CUDA graph the kernel
+  // boundary is already cheap and the programmatic edge measured slower, so
+  // captured launches are plain (griddepcontrol.wait is then a no-op).
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = cap == cudaStreamCaptureStatusNone ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, combine_kernel, p, num_splits, lse_accum, o_accum);
 }
 
 cudaError_t launch_gather_dequant(int layout, const void* kv, int num_blocks, int page_block_size,

@@ -41,6 +41,7 @@
 #include <cuda_bf16.h>
 
 #include <cstddef>
+#include <cstdlib>
 
 #include "dsv4b_internal.cuh"
 #include "dsv4b_kernels.h"
@@ -964,6 +965,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t p_s = base_addr + SP::kPOff;
 
   const int warp = threadIdx.x >> 5;
+  // A dependent combine launch may be scheduled now; it waits in-kernel
+  // for this grid's completion (griddepcontrol.wait).
+  asm volatile("griddepcontrol.launch_dependents;");
   const dsv4b_sched_meta sm = sched[blockIdx.x];
   const int g = blockIdx.y;
 
@@ -1046,17 +1050,17 @@ cudaError_t set_smem_attr() {
   return cudaSuccess;
 }
 
-// Whether clusters of c decode CTAs can be resident at all on this device
+// How many clusters of c decode CTAs can be resident at once on this device
 // (one CTA per SM, clusters confined to a GPC).  Cached per device.
 template <int L>
-bool cluster_fits(int c) {
-  static signed char cache[64][4] = {};  // 0 unknown, 1 yes, -1 no; index log2(c) - 1
+int clusters_resident(int c) {
+  static int cache[64][4] = {};  // 0 unknown, else count + 1; index log2(c) - 1
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   const int k = c == 2 ? 0 : c == 4 ? 1 : 2;
   if (cache[dev][k] == 0) {
-    bool ok = set_smem_attr<L>() == cudaSuccess;
-    if (ok) {
+    int n = 0;
+    if (set_smem_attr<L>() == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(c, 1, 1);
       cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1068,13 +1072,12 @@ bool cluster_fits(int c) {
       attr.val.clusterDim.z = 1;
       cfg.attrs = &attr;
       cfg.numAttrs = 1;
-      int n = 0;
-      ok = cudaOccupancyMaxActiveClusters(&n, sparse_decode_kernel<L>, &cfg) == cudaSuccess && n >= 1;
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_decode_kernel<L>, &cfg) != cudaSuccess) n = 0;
       cudaGetLastError();  // a refused query leaves no sticky error
     }
-    cache[dev][k] = ok ? 1 : -1;
+    cache[dev][k] = n + 1;
   }
-  return cache[dev][k] > 0;
+  return cache[dev][k] - 1;
 }
 
 template <int L>
@@ -1103,19 +1106,33 @@ cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_m
 
 }  // namespace
 
-// Cluster size of the plan for this batch: the largest power of two C <= 8
-// with b*s_q*C <= num_sm_parts and C <= the most tiles a query row can
-// have, whose clusters fit on the device; 1 = no cluster (split partials
-// are merged by the combine kernel instead).
+// Cluster size of the plan for this batch; 1 = no cluster (split partials
+// are merged by the combine kernel).  Candidates are C in {8, 4, 2} with
+// b*s_q*C <= num_sm_parts, C <= the most tiles a row can have, and every
+// cluster of the launch resident at once (one wave).  The largest such C
+// gives k_c = ceil(tiles / C) tiles per CTA; it is used unless the
+// row-aligned plan would give its parts fewer tiles (k_r), since a tile
+// (~7 us) costs more than the combine step that plan adds.
 int plan_cluster_size(const dsv4b_decode_params& p, int num_sm_parts) {
+  static const bool clusters_off = [] {
+    const char* e = getenv("DSV4B_CLUSTER");  // "0": never use the cluster plan
+    return e && e[0] == '0';
+  }();
+  if (clusters_off) return 1;
   const int64_t rows = (int64_t)p.b * p.s_q;
+  const int groups = (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta;
   const int tiles_max = (p.topk + kTileTokens - 1) / kTileTokens +
                         (p.extra_kv ? (p.extra_topk + kTileTokens - 1) / kTileTokens : 0);
+  if (rows > num_sm_parts) return 1;
+  int kr = 1;  // row-aligned cap: smallest t with rows * ceil(tiles / t) <= parts
+  while (rows * ((tiles_max + kr - 1) / kr) > num_sm_parts) ++kr;
   for (int c = 8; c >= 2; c >>= 1) {
     if (rows * c > num_sm_parts || c > tiles_max) continue;
-    const bool fits = p.layout == DSV4B_LAYOUT_V32 ? cluster_fits<DSV4B_LAYOUT_V32>(c)
-                                                   : cluster_fits<DSV4B_LAYOUT_MODEL1>(c);
-    if (fits) return c;
+    const int resident = p.layout == DSV4B_LAYOUT_V32 ? clusters_resident<DSV4B_LAYOUT_V32>(c)
+                                                      : clusters_resident<DSV4B_LAYOUT_MODEL1>(c);
+    if (resident < rows * groups) continue;
+    const int kc = (tiles_max + c - 1) / c;
+    return kc <= kr ? c : 1;
   }
   return 1;
 }

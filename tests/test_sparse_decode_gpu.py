@@ -335,3 +335,41 @@ def test_partition_shards_match_full_decode(mode):
     got_lse = torch.cat([l for _, l in outs], dim=0 if mode == "batch" else 1)
     torch.testing.assert_close(got.float(), full_out.float(), atol=OUT_ATOL, rtol=OUT_RTOL)
     torch.testing.assert_close(got_lse, full_lse, atol=LSE_ATOL, rtol=LSE_RTOL)
+
+
+@pytest.mark.parametrize("b,topk", [(1, 2048), (4, 1024), (33, 512), (200, 256)])
+def test_cuda_graph_capture_and_replay(b, topk):
+    """The whole step (flash_mla_with_kvcache with a reused FlashMLASchedMeta)
+    is captured once in a CUDA graph and replayed with new q / indices in the
+    same buffers, as SGLang's decode graphs do; each replay matches the
+    oracle.  The first call (workspace, scheduler, cluster set-up) runs
+    before capture."""
+    import deepseek_v4_kernel as dk
+    kc = _kc()
+    spec = kc.BatchSpec(b=b, s_q=1, h_q=64, topk=topk, ctx=4096, page_block=64, invalid_tail=3, seed=51)
+    bt = kc.make_batch(spec)
+    q_buf, idx_buf = bt.q.clone(), bt.indices.clone()
+    sched, _ = dk.get_mla_metadata()
+
+    def step():
+        return dk.flash_mla_with_kvcache(q_buf, bt.kv, None, None, 512, sched, softmax_scale=bt.sm_scale,
+                                         is_fp8_kvcache=True, indices=idx_buf, attn_sink=bt.attn_sink)
+
+    step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out_g, lse_g = step()
+    for seed in (52, 53):
+        other = kc.make_batch(kc.BatchSpec(**{**spec.__dict__, "seed": seed}))
+        q_buf.copy_(other.q)
+        idx_buf.copy_(other.indices)  # same cache geometry, so valid rows of bt.kv
+        g.replay()
+        torch.cuda.synchronize()
+        ref_out, ref_lse = oracle_for(q_buf, bt.kv, idx_buf, None, bt.attn_sink, bt.sm_scale, "v32")
+        assert_matches(out_g, lse_g, ref_out, ref_lse)
