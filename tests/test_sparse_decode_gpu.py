@@ -373,3 +373,42 @@ def test_cuda_graph_capture_and_replay(b, topk):
         torch.cuda.synchronize()
         ref_out, ref_lse = oracle_for(q_buf, bt.kv, idx_buf, None, bt.attn_sink, bt.sm_scale, "v32")
         assert_matches(out_g, lse_g, ref_out, ref_lse)
+
+
+@pytest.mark.parametrize("layout,b,s_q,h_q,topk,cluster", [
+    ("v32", 32, 1, 64, 2048, True),      # config-1 shape: clusters of 4
+    ("model1", 32, 1, 64, 1024, True),   # MODEL1 under the cluster plan
+    ("v32", 8, 2, 128, 1024, True),      # s_q 2, two head groups, clusters
+    ("v32", 5, 1, 96, 700, False),       # h_q not a multiple of 64, clusters off
+    ("model1", 3, 2, 16, 333, False),    # small head count, ragged top-k
+])
+def test_plans_and_layouts_match_oracle(layout, b, s_q, h_q, topk, cluster):
+    """Every plan the scheduler can pick (cluster merge or split + combine)
+    gives the oracle's answer for both layouts, with a -1 tail, sinks and
+    topk_length."""
+    from deepseek_v4_kernel import ops
+    spec = _kc().BatchSpec(b=b, s_q=s_q, h_q=h_q, topk=topk, ctx=8192, page_block=64, layout=layout,
+                           invalid_tail=11, seed=61)
+    bt = _kc().make_batch(spec)
+    tk = torch.randint(1, topk + 1, (b,), dtype=torch.int32, device="cuda")
+    parts = ops.num_sm_parts(torch.device("cuda", 0), h_q)
+    c = ops.plan_cluster_size(_params(bt, tk), parts)
+    assert (c > 1) == cluster, c
+    out, lse, _, _ = _run(bt, topk_length=tk)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, tk, bt.attn_sink, bt.sm_scale, layout)
+    assert_matches(out, lse, ref_out, ref_lse)
+
+
+def test_extra_kv_sidecar_cluster_plan():
+    """The SWA sidecar under the default (cluster) plan: the extra tiles join
+    the split of each row."""
+    kc = _kc()
+    spec = kc.BatchSpec(b=16, s_q=1, h_q=64, topk=1024, ctx=4096, page_block=64, seed=71)
+    bt = kc.make_batch(spec)
+    ex = kc.make_batch(kc.BatchSpec(b=16, s_q=1, h_q=64, topk=256, ctx=1024, page_block=64, seed=72))
+    etk = torch.randint(0, 257, (16,), dtype=torch.int32, device="cuda")
+    extra = (ex.kv, ex.indices, etk)
+    out, lse, _, _ = _run(bt, extra=extra)
+    ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink, bt.sm_scale, "v32",
+                                  extra=extra)
+    assert_matches(out, lse, ref_out, ref_lse)

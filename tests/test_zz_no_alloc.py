@@ -58,11 +58,13 @@ def _both_paths(bt):
 def test_noalloc_matches_workspace_entry_point_twice():
     from deepseek_v4_kernel import kvcache
     torch.cuda.set_device(0)
-    # two different batches, both split over several scheduler parts
+    # different batches, each split over several scheduler parts
     specs = [
         kvcache.BatchSpec(b=4, s_q=1, h_q=64, topk=2048, ctx=32768, page_block=256, seed=31),
         kvcache.BatchSpec(b=3, s_q=2, h_q=128, topk=1000, ctx=8192, page_block=64,
                           invalid_tail=9, seed=32),
+        # 32 rows: the rows are merged inside thread-block clusters
+        kvcache.BatchSpec(b=32, s_q=1, h_q=64, topk=2048, ctx=8192, page_block=64, seed=33),
     ]
     for spec in specs:
         outs = _both_paths(kvcache.make_batch(spec))
