@@ -64,6 +64,14 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
+    ap.add_argument("--op", choices=["decode", "kv_write"], default="decode",
+                    help="kv_write: the KV-cache writer (quantise + scatter) instead of the decode step")
+    ap.add_argument("--kv-layout", choices=["v32", "model1"], default="v32")
+    ap.add_argument("--tokens", type=int, default=131072, help="kv_write: tokens written per step")
+    ap.add_argument("--pages", type=int, default=16384, help="kv_write: cache pages of 256 tokens")
+    ap.add_argument("--slots", choices=["paged", "random"], default="paged",
+                    help="kv_write: 'paged' = consecutive slots inside randomly placed pages (a prefill "
+                         "chunk through a block table); 'random' = every token at a random slot")
     return ap.parse_args()
 
 
@@ -452,6 +460,118 @@ def run_ours(args, spec, world, rank, local_rank):
             f.write(json.dumps(line) + "\n")
 
 
+def run_kv_write(args):
+    """One step = one dsv4b_kv_cache_write of --tokens bf16 tokens (a
+    prefill chunk) into BASELINE config 1's cache geometry (16,384 pages of
+    256 tokens) at random distinct slots.  Per step the kernel reads
+    1,152 (V32) / 1,024 (MODEL1) B of bf16 per token plus an 8-B slot and
+    writes 656 / 584 B, more than L2 holds, so no flush is needed."""
+    import numpy as np
+    import torch
+
+    from deepseek_v4_kernel import _lib, cache_ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    n, page, nb = args.tokens, 256, args.pages
+    v32 = args.kv_layout == "v32"
+    g = torch.Generator(device=device).manual_seed(0)
+    nope = torch.randn(n, 512 if v32 else 448, generator=g, device=device).to(torch.bfloat16)
+    rope = torch.randn(n, 64, generator=g, device=device).to(torch.bfloat16)
+    if args.slots == "random":
+        slots = torch.randperm(nb * page, generator=g, device=device)[:n].contiguous()
+    else:
+        pages = torch.randperm(nb, generator=g, device=device)[: -(-n // page)]
+        t = torch.arange(n, device=device)
+        slots = (pages[t // page] * page + t % page).contiguous()
+    if v32:
+        cache = torch.zeros(nb, page, 1, 656, dtype=torch.uint8, device=device)
+        layout, bs = _lib.LAYOUT_V32, None
+    else:
+        cache = torch.zeros(nb, page * 584, dtype=torch.uint8, device=device)
+        layout, bs = _lib.LAYOUT_MODEL1, page
+    per_tok_read = (1024 if v32 else 896) + 128 + 8
+    per_tok_write = 656 if v32 else 584
+    alg = n * (per_tok_read + per_tok_write)
+
+    def step():
+        cache_ops.kv_cache_write(layout, nope, rope, slots, cache, block_size=bs)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # The K timed launches are one CUDA graph, so they run back to back on
+    # the device whatever the host-side cost of a Python call.
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for _ in range(args.steps):
+                step()
+    torch.cuda.current_stream(device).wait_stream(cap)
+    graph.replay()          # warm replay
+    torch.cuda.synchronize()
+    clk = ClockSampler(0)
+    clk.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    graph.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    t_step_ms = t0.elapsed_time(t1) / args.steps
+    t_kernel_ms = t_step_ms
+    hbm_peak, _, peak_src = measured_peaks()
+    ach = alg / (t_kernel_ms * 1e-3) / 1e9
+
+    # CPU baseline: the oracle on a bounded sample of the same tokens
+    from oracle import kv_writer_oracle as KW
+    sample = min(n, 16384)
+    nb_s = -(-sample // page)
+    arena = np.zeros((nb_s, page * (656 if v32 else 584)), np.uint8)
+    nb_bits = nope[:sample].cpu().view(torch.int16).numpy().view(np.uint16)
+    rp_bits = rope[:sample].cpu().view(torch.int16).numpy().view(np.uint16)
+    sl = np.arange(sample)
+    c0 = time.perf_counter()
+    KW.kv_cache_write(args.kv_layout, arena, page, nb_bits, rp_bits, sl)
+    cpu_s = time.perf_counter() - c0
+    line = {
+        "metric": "kv_cache_write_us_per_step",
+        "value": round(t_step_ms * 1e3, 2),
+        "unit": "us/step",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step_ms, 5),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic (seeded N(0,1) bf16 tokens, %s slots)" % (
+            "random distinct" if args.slots == "random" else "page-consecutive, random physical pages"),
+        "config": {"workload": f"kv_write {args.kv_layout} ({args.slots} slots): {n} tokens into {nb} pages x 256"
+                               + (" (config 1 cache geometry)" if nb == 16384 else ""),
+                   "l2": f"no flush: {alg / 1e6:.0f} MB moved per step, above L2 size"},
+        "kernel_us": round(t_kernel_ms * 1e3, 2),
+        "timing": "one CUDA graph of `steps` writer launches, CUDA events around its replay",
+        "tokens_per_s": round(n / (t_step_ms * 1e-3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(ach / hbm_peak, 4), "traffic": None, "peak_source": peak_src,
+                     "kernel": "kv_write_%s_kernel" % args.kv_layout,
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "cpu_baseline": {"value": round(cpu_s / sample * n * 1e6, 1), "unit": "us/step", "cores": 1,
+                         "kind": "port", "sample": f"oracle/kv_writer_oracle.py on {sample} of the {n} "
+                                                   f"tokens, scaled to {n}"},
+    }
+    print(json.dumps(line), flush=True)
+    if args.json_out:
+        with open(args.json_out, "w") as f:
+            f.write(json.dumps(line) + "\n")
+
+
 def run_sweep(args):
     """b in {1..32} x context in {8K..300K}, h_q 64, top-k
     2048; the whole step (flash_mla_with_kvcache with a reused
@@ -523,6 +643,10 @@ def run_sweep(args):
 
 def main():
     args = parse()
+    if args.op == "kv_write":
+        if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
+            run_kv_write(args)
+        return
     if args.config == 3 and args.impl == "ours":
         run_sweep(args)
         return

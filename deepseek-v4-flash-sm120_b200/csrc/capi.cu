@@ -257,6 +257,41 @@ int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks, int page_bl
                                               static_cast<cudaStream_t>(stream)));
 }
 
+int dsv4b_kv_cache_write(int layout, const void* nope, int64_t stride_nope, const void* rope,
+                         int64_t stride_rope, const void* slot_mapping, int slot_bytes, int64_t n,
+                         void* kv, int num_blocks, int page_block_size, int64_t stride_kv_block,
+                         int64_t stride_kv_row, void* stream) {
+  if (layout != DSV4B_LAYOUT_V32 && layout != DSV4B_LAYOUT_MODEL1) return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = check_cache(layout, kv, num_blocks, page_block_size, stride_kv_block, stride_kv_row);
+  if (rc) return rc;
+  if (n < 0 || n > (int64_t)INT_MAX || (slot_bytes != 4 && slot_bytes != 8)) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (n == 0) return DSV4B_OK;
+  const int64_t nope_cols = layout == DSV4B_LAYOUT_V32 ? 512 : 448;
+  if (!nope || !rope || !slot_mapping || !aligned(nope, 16) || !aligned(rope, 16) ||
+      !aligned(slot_mapping, slot_bytes))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (stride_nope % 8 || stride_rope % 8 || (n > 1 && (stride_nope < nope_cols || stride_rope < 64)))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((rc = current_arch_ok())) return rc;
+  return cuda_rc(dsv4b::launch_kv_cache_write(layout, nope, stride_nope, rope, stride_rope, slot_mapping,
+                                              slot_bytes, n, kv, num_blocks, page_block_size,
+                                              stride_kv_block, stride_kv_row,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_kv_cache_write_status(int* flags, void* stream) {
+  if (!flags) return DSV4B_ERR_INVALID_ARGUMENT;
+  return cuda_rc(dsv4b::read_kv_write_status(flags, static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_kv_write_selftest(const float* scales, int n_scales, unsigned long long* mismatches,
+                            void* stream) {
+  if (!scales || n_scales <= 0 || !mismatches) return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
+  if (rc) return rc;
+  return cuda_rc(dsv4b::launch_div_selftest(scales, n_scales, mismatches, static_cast<cudaStream_t>(stream)));
+}
+
 int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
                                 const int32_t* num_splits, int num_sm_parts, void* stream) {
   int rc = check_params(p);

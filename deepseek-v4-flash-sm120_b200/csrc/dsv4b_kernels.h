@@ -37,4 +37,13 @@ cudaError_t launch_gather_dequant(int layout, const void* kv, int num_blocks, in
                                   const int32_t* indices, int n, void* out_bf16,
                                   cudaStream_t stream);
 
+cudaError_t launch_kv_cache_write(int layout, const void* nope, int64_t stride_nope, const void* rope,
+                                  int64_t stride_rope, const void* slots, int slot_bytes, int64_t n,
+                                  void* kv, int num_blocks, int page, int64_t stride_block,
+                                  int64_t stride_row, cudaStream_t stream);
+
+cudaError_t read_kv_write_status(int* flags, cudaStream_t stream);
+cudaError_t launch_div_selftest(const float* scales, int n_scales, unsigned long long* mismatches,
+                                cudaStream_t stream);
+
 }  // namespace dsv4b

@@ -78,6 +78,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Arrive once on `bar` and add `bytes` to the transaction count the
+// current phase waits for (the bulk copies that complete_tx on it).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Untiled bulk copy of `bytes` from global memory to this CTA's shared
+// memory (both addresses 16-byte aligned, bytes a multiple of 16); its
+// completion is counted as transaction bytes on `bar`.  No multicast.
+__device__ __forceinline__ void bulk_g2s(uint32_t saddr, const void* gptr, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   saddr),
+               "l"(gptr), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -31,7 +31,8 @@ EXPORTED = (
     "dsv4b_num_sm_parts", "dsv4b_workspace_bytes", "dsv4b_get_mla_metadata",
     "dsv4b_sparse_decode", "dsv4b_combine", "dsv4b_sparse_decode_partial",
     "dsv4b_gather_dequant", "dsv4b_read_kernel_status", "dsv4b_sparse_decode_noalloc",
-    "dsv4b_plan_cluster_size",
+    "dsv4b_plan_cluster_size", "dsv4b_kv_cache_write",
+    "dsv4b_kv_cache_write_status", "dsv4b_kv_write_selftest",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -90,6 +91,10 @@ def _load():
     lib.dsv4b_combine.argtypes = [P, _vp, ctypes.c_int, _vp, ctypes.c_size_t, _vp]
     lib.dsv4b_gather_dequant.argtypes = [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int,
                                          _i64, _i64, _vp, ctypes.c_int, _vp, _vp]
+    lib.dsv4b_kv_cache_write.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp, ctypes.c_int, _i64,
+                                         _vp, ctypes.c_int, ctypes.c_int, _i64, _i64, _vp]
+    lib.dsv4b_kv_write_selftest.argtypes = [_vp, ctypes.c_int, _vp, _vp]
+    lib.dsv4b_kv_cache_write_status.argtypes = [ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]
     lib.dsv4b_read_kernel_status.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int), _vp]
     return lib

@@ -4,8 +4,9 @@ Quantisers write the two page formats the decode kernel reads:
 
 * V32 (DeepSeek-V3.2, FlashMLA FP8 sparse; vLLM flash_mla_interface.py:95-101):
   656 B per token, token-contiguous: 512 x e4m3 (latent / scale of its
-  128-column tile), 4 x fp32 scales (amax / 448 per 128 columns), 64 x bf16
-  RoPE.  Pages are [page_block, 1, 656].
+  128-column tile), 4 x fp32 scales (max(amax / 448, FLT_MIN) per 128
+  columns, vLLM's fp8_ds_mla rule), 64 x bf16 RoPE.  Pages are
+  [page_block, 1, 656].
 * MODEL1 (DeepSeek-V4-Flash; reference tests/reference.py:7-19): per page
   page_block x 576 B rows [448 x e4m3 | 64 x bf16 RoPE], then page_block x
   8 B of UE8M0 exponents (7 used: 2^e per 64 columns, + 1 pad).
@@ -25,7 +26,8 @@ from typing import Optional
 import torch
 
 FP8_MAX = 448.0
-AMAX_FLOOR = 1e-4  # an all-zero tile gets scale 1e-4/448 instead of 0
+AMAX_FLOOR = 1e-4  # MODEL1: an all-zero tile gets scale 2^ceil(log2(1e-4/448))
+FLT_MIN = 1.17549435e-38  # V32: an all-zero tile gets scale FLT_MIN
 
 
 def _to_e4m3_bytes(x: torch.Tensor) -> torch.Tensor:
@@ -35,8 +37,11 @@ def _to_e4m3_bytes(x: torch.Tensor) -> torch.Tensor:
 def quantize_v32(latent: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
     """latent [N, 512] float, rope [N, 64] bf16 -> uint8 [N, 656]."""
     n = latent.shape[0]
-    lt = latent.float().view(n, 4, 128)
-    scale = lt.abs().amax(dim=-1).clamp_min(AMAX_FLOOR) / FP8_MAX          # [N, 4] fp32
+    lt = latent.to(torch.bfloat16).float().view(n, 4, 128)
+    amax = lt.abs().amax(dim=-1)
+    # divide by a tensor: torch's CUDA division by a Python scalar multiplies
+    # by the reciprocal, which is not the correctly rounded quotient
+    scale = (amax / torch.full_like(amax, FP8_MAX)).clamp_min(FLT_MIN)     # [N, 4] fp32
     q8 = _to_e4m3_bytes(lt / scale.unsqueeze(-1)).view(n, 512)
     sc = scale.contiguous().view(torch.uint8).view(n, 16)
     rp = rope.to(torch.bfloat16).contiguous().view(torch.uint8).view(n, 128)

@@ -179,6 +179,49 @@ DSV4B_API int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks,
                          int64_t stride_kv_row, const int32_t* indices, int n,
                          void* out_bf16, void* stream);
 
+/* KV-cache writer: quantise n bf16 tokens into the cache's FP8 format and
+ * scatter them to their slots (flat page * page_block_size + offset).
+ *   layout V32:    nope = latent [n, 512], rope = [n, 64]; 656-B records
+ *                  [512 e4m3 | 4 fp32 scales | 64 bf16 RoPE] at
+ *                  page * stride_kv_block + offset * stride_kv_row;
+ *                  scale = max(amax / 448, FLT_MIN) per 128 columns
+ *                  (vLLM's fp8_ds_mla rule; an all-zero tile gets FLT_MIN).
+ *   layout MODEL1: nope = [n, 448], rope = [n, 64] (for a [n, 512] k, pass
+ *                  k and k + 448 with the same stride); per page P x 576-B
+ *                  rows [448 e4m3 | 64 bf16 RoPE] then P x 8 UE8M0 bytes,
+ *                  scale = 2^ceil(log2(max(amax, 1e-4) / 448)) per 64
+ *                  columns (stride_kv_row is ignored).
+ * e4m3 values are x / scale clamped to +-448, rounded to nearest even.
+ * Element row strides (multiples of 8), 16-byte aligned rows.  slot_bytes
+ * is 8 (int64 slots, vLLM's slot_mapping) or 4 (int32).  Tokens whose slot
+ * is negative or >= num_blocks * page_block_size are skipped.
+ * The producer of the bytes the decode path reads: SGLang's
+ * quant_k_cache_v4 (tests/reference.py:45-58 unpacks its output); same
+ * bytes as vLLM's quantize_and_insert_k_cache (MODEL1) and
+ * concat_and_cache_mla with kv_cache_dtype "fp8_ds_mla" (V32). */
+DSV4B_API int dsv4b_kv_cache_write(int layout, const void* nope, int64_t stride_nope,
+                                   const void* rope, int64_t stride_rope,
+                                   const void* slot_mapping, int slot_bytes, int64_t n,
+                                   void* kv, int num_blocks, int page_block_size,
+                                   int64_t stride_kv_block, int64_t stride_kv_row,
+                                   void* stream);
+
+/* Reads (and clears) this device's status word of dsv4b_kv_cache_write
+ * into *flags (0 = no error; 1 = a kernel wait hit its time limit and the
+ * write is incomplete).  Synchronises `stream`.  New: the reference has
+ * no writer. */
+DSV4B_API int dsv4b_kv_cache_write_status(int* flags, void* stream);
+
+/* Self-test of the V32 writer's quotient x / scale (an FMA refinement of
+ * one reciprocal per scale tile instead of a division per element): every
+ * finite bf16 x against each of the n_scales device floats in `scales`
+ * with |x| <= 448 * scale (the writer's domain).  Adds to mismatches[0]
+ * (device uint64[2]) the e4m3 bytes that differ from those of the
+ * hardware division, to mismatches[1] the differing fp32 quotients of
+ * normal magnitude.  For tests. */
+DSV4B_API int dsv4b_kv_write_selftest(const float* scales, int n_scales,
+                                      unsigned long long* mismatches, void* stream);
+
 /* Reads (and clears) the kernel status word kept in the workspace into
  * *flags (0 = no error).  Synchronises `stream`. */
 DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
