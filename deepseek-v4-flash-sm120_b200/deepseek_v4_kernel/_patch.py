@@ -5,7 +5,9 @@ Same mechanism as the reference (deepseek_v4_kernel/_patch.py:161-265):
 ``flash_mla.flash_mla_interface`` attribute) and vLLM's vendored copy
 ``vllm.third_party.flashmla.flash_mla_interface.flash_mla_with_kvcache``
 with a wrapper that takes the sparse + FP8 + bf16-q path on sm_100 GPUs
-and defers everything else to the original function.
+and defers everything else to the original function.  It also wraps
+SGLang's two DeepSeek-V4 indexer fallbacks so that a 2-D ``seq_lens``
+reaches them 1-D (reference ``_patch.py:199-236``).
 
 Environment (own prefix, reference style): ``DSV4B_KERNEL_TRACE=1`` logs
 each gating decision; ``DSV4B_KERNEL_STRICT=1`` re-raises errors of the
@@ -120,6 +122,51 @@ def _patch_vllm_pkg() -> bool:
     return patch_module(vfmi, vpkg)
 
 
+def squeeze_seq_lens_wrapper(original: Callable) -> Callable:
+    """Wrap an indexer-logits function ``f(q_fp8, kvcache_fp8, weight,
+    seq_lens, ...)`` so that a ``[b, 1]`` ``seq_lens`` arrives as ``[b]``.
+
+    SGLang's DeepSeek-V4 C4 indexer unsqueezes ``seq_lens`` to 2-D for
+    DeepGEMM's signature but its fallbacks assert 1-D; the reference patches
+    both fallbacks the same way (deepseek_v4_kernel/_patch.py:199-236).  On
+    B200 SGLang normally takes DeepGEMM and never reaches the fallbacks; the
+    patch keeps them usable when it does (e.g. DeepGEMM missing)."""
+    def wrapper(q_fp8, kvcache_fp8, weight, seq_lens, *args, **kwargs):
+        if isinstance(seq_lens, torch.Tensor) and seq_lens.dim() == 2 and seq_lens.shape[-1] == 1:
+            seq_lens = seq_lens.squeeze(-1).contiguous()
+        return original(q_fp8, kvcache_fp8, weight, seq_lens, *args, **kwargs)
+
+    wrapper.__wrapped__ = original  # type: ignore[attr-defined]
+    wrapper.__dsv4b_patched__ = True  # type: ignore[attr-defined]
+    return wrapper
+
+
+# (module, attribute) of SGLang's indexer fallbacks that get the wrapper.
+INDEXER_FALLBACKS = (
+    ("sglang.srt.layers.attention.nsa.tilelang_kernel", "tilelang_fp8_paged_mqa_logits"),
+    ("sglang.srt.layers.attention.compressed.indexer", "fp8_paged_mqa_logits_torch"),
+)
+
+
+def _patch_sglang_indexer_fallbacks() -> int:
+    """Wrap the SGLang indexer fallbacks that are importable; returns how
+    many are (now) wrapped."""
+    import importlib
+    n = 0
+    for mod_name, attr in INDEXER_FALLBACKS:
+        try:
+            mod = importlib.import_module(mod_name)
+        except Exception:
+            continue
+        fn = getattr(mod, attr, None)
+        if fn is None:
+            continue
+        if not getattr(fn, "__dsv4b_patched__", False):
+            setattr(mod, attr, squeeze_seq_lens_wrapper(fn))
+        n += 1
+    return n
+
+
 def install() -> bool:
     """Install the patch (idempotent).  Returns True if anything was patched."""
     global _INSTALLED
@@ -129,6 +176,7 @@ def install() -> bool:
         return False
     patched = _patch_flash_mla_pkg()
     patched = _patch_vllm_pkg() or patched
+    _patch_sglang_indexer_fallbacks()
     if not patched:
         _log.warning("deepseek_v4_kernel: neither flash_mla nor vllm.third_party.flashmla "
                      "was importable; nothing patched.")
