@@ -64,8 +64,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
-    ap.add_argument("--op", choices=["decode", "kv_write"], default="decode",
-                    help="kv_write: the KV-cache writer (quantise + scatter) instead of the decode step")
+    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits"], default="decode",
+                    help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
+                         "logits (fp8_paged_mqa_logits) over config 1's contexts")
+    ap.add_argument("--next-n", type=int, default=1, help="mqa_logits: query rows per request")
     ap.add_argument("--kv-layout", choices=["v32", "model1"], default="v32")
     ap.add_argument("--tokens", type=int, default=131072, help="kv_write: tokens written per step")
     ap.add_argument("--pages", type=int, default=16384, help="kv_write: cache pages of 256 tokens")
@@ -572,6 +574,107 @@ def run_kv_write(args):
             f.write(json.dumps(line) + "\n")
 
 
+def run_mqa_logits(args):
+    """One step = one fp8_paged_mqa_logits call over b requests x ctx
+    positions (default BASELINE config 1: b 32, 131,072 positions, 64
+    heads x 128, pages of 64), K launches in one CUDA graph.  Per position
+    the kernel reads 128 e4m3 values + a 4-B scale and writes next_n 4-B
+    logits; the 554 MB cache is above L2 size, so no flush is needed."""
+    import numpy as np
+    import torch
+
+    from deepseek_v4_kernel import indexer
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B = args.batch or 32
+    ctx_len = args.ctx or 131072
+    H, P, nn = 64, 64, args.next_n
+    pages = -(-ctx_len // P)
+    nb = B * pages
+    g = torch.Generator(device=device).manual_seed(0)
+    arena = torch.empty(nb, P * 132, dtype=torch.uint8, device=device)
+    arena[:, :P * 128] = torch.randn(nb, P * 128, generator=g, device=device).to(torch.float8_e4m3fn).view(torch.uint8)
+    arena[:, P * 128:] = (torch.rand(nb, P, generator=g, device=device) * 0.1).view(torch.uint8).view(nb, P * 4)
+    kv = arena.view(nb, P, 1, 132)
+    q = torch.randn(B, nn, H, 128, generator=g, device=device).to(torch.float8_e4m3fn)
+    w = torch.randn(B * nn, H, generator=g, device=device)
+    ctx = torch.full((B,), ctx_len, dtype=torch.int32, device=device)
+    bt = torch.randperm(nb, generator=g, device=device).view(B, pages).int()
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    sched = indexer.get_paged_mqa_logits_metadata(ctx, P, sms)
+    out = torch.empty(B * nn, ctx_len, dtype=torch.float32, device=device)
+
+    def step():
+        indexer.fp8_paged_mqa_logits(q, kv, w, ctx, bt, sched, ctx_len, True, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for _ in range(args.steps):
+                step()
+    torch.cuda.current_stream(device).wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    clk = ClockSampler(0)
+    clk.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    graph.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    t_ms = t0.elapsed_time(t1) / args.steps
+    positions = B * ctx_len
+    alg = positions * 132 + positions * nn * 4 + q.numel() + w.numel() * 4 + bt.numel() * 4
+    flops = 2.0 * nn * H * 128 * positions
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    ach = alg / (t_ms * 1e-3) / 1e9
+
+    from oracle import mqa_logits_oracle as M
+    c0 = time.perf_counter()
+    M.fp8_paged_mqa_logits(q[:1].view(torch.uint8).cpu().numpy(), arena[bt[0].long()].cpu().numpy(),
+                           w[:nn].cpu().numpy(), np.array([ctx_len]), np.arange(pages)[None, :], P, ctx_len)
+    cpu_s = time.perf_counter() - c0
+    line = {
+        "metric": "mqa_logits_us_per_step",
+        "value": round(t_ms * 1e3, 2),
+        "unit": "us/step",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_ms, 5),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8-e4m3 (fp32 accumulate)",
+        "data": "synthetic (seeded N(0,1) e4m3 q and cache, uniform scales, random page tables)",
+        "config": {"workload": f"mqa_logits: b{B} next_n{nn} h{H} d128 ctx{ctx_len} page{P} (config 1 contexts)",
+                   "l2": f"no flush: {alg / 1e6:.0f} MB per step, above L2 size"},
+        "timing": "one CUDA graph of `steps` launches, CUDA events around its replay",
+        "positions_per_s": round(positions / (t_ms * 1e-3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(ach / hbm_peak, 4), "traffic": None, "peak_source": peak_src,
+                     "kernel": "mqa_logits_kernel", "algorithmic_bytes_per_launch": alg,
+                     "algorithmic_flops_per_launch": flops,
+                     "tensor_frac_of_bf16_peak": round(flops / (t_ms * 1e-3) / 1e12 / tc_peak, 4)},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "cpu_baseline": {"value": round(cpu_s * B * 1e6, 1), "unit": "us/step", "cores": 1, "kind": "port",
+                         "sample": f"oracle/mqa_logits_oracle.py (float64 numpy) on 1 of the {B} requests, "
+                                   f"scaled to {B}"},
+    }
+    print(json.dumps(line), flush=True)
+    if args.json_out:
+        with open(args.json_out, "w") as f:
+            f.write(json.dumps(line) + "\n")
+
+
 def run_sweep(args):
     """b in {1..32} x context in {8K..300K}, h_q 64, top-k
     2048; the whole step (flash_mla_with_kvcache with a reused
@@ -643,9 +746,9 @@ def run_sweep(args):
 
 def main():
     args = parse()
-    if args.op == "kv_write":
+    if args.op in ("kv_write", "mqa_logits"):
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            run_kv_write(args)
+            (run_kv_write if args.op == "kv_write" else run_mqa_logits)(args)
         return
     if args.config == 3 and args.impl == "ours":
         run_sweep(args)

@@ -292,6 +292,44 @@ int dsv4b_kv_write_selftest(const float* scales, int n_scales, unsigned long lon
   return cuda_rc(dsv4b::launch_div_selftest(scales, n_scales, mismatches, static_cast<cudaStream_t>(stream)));
 }
 
+int dsv4b_mqa_logits_metadata(const int32_t* context_lens, int b, int num_sms, int32_t* sched, void* stream) {
+  if (!context_lens || !sched || b <= 0 || b > dsv4b::kMaxMqaRequests || num_sms <= 0 || num_sms > 65535)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
+  if (rc) return rc;
+  return cuda_rc(dsv4b::launch_mqa_metadata(context_lens, b, num_sms, sched, static_cast<cudaStream_t>(stream)));
+}
+
+int dsv4b_fp8_paged_mqa_logits(const dsv4b_mqa_logits_params* p, const int32_t* sched, int num_sms,
+                               void* stream) {
+  if (!p || !sched || num_sms <= 0 || num_sms > 65535) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->b <= 0 || p->b > dsv4b::kMaxMqaRequests || p->next_n <= 0 || p->d != 128) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->h != 32 && p->h != 64 && p->h != 128) return DSV4B_ERR_UNSUPPORTED;
+  const int n = p->next_n * p->h;
+  if (n != 32 && n != 64 && n != 128 && n != 256) return DSV4B_ERR_UNSUPPORTED;
+  const int P = p->page_block_size;
+  if (P != 32 && P != 64 && P != 128) return DSV4B_ERR_UNSUPPORTED;
+  if (!p->q || !p->kv || !p->weights || !p->context_lens || !p->block_table || !p->logits)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->q, 16) || !aligned(p->kv, 16) || !aligned(p->weights, 16) || !aligned(p->logits, 4))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->num_blocks <= 0 || p->stride_kv_block % 16 || p->stride_kv_block < (int64_t)P * 132)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->max_model_len < 0 || p->stride_logits < p->max_model_len || p->stride_block_table < 0)
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
+  if (rc) return rc;
+  int bad = 0;
+  const cudaError_t e = dsv4b::launch_mqa_logits(*p, sched, num_sms, static_cast<cudaStream_t>(stream), &bad);
+  if (bad) return DSV4B_ERR_INVALID_ARGUMENT;
+  return cuda_rc(e);
+}
+
+int dsv4b_mqa_logits_status(int* flags, void* stream) {
+  if (!flags) return DSV4B_ERR_INVALID_ARGUMENT;
+  return cuda_rc(dsv4b::read_mqa_status(flags, static_cast<cudaStream_t>(stream)));
+}
+
 int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p, const dsv4b_sched_meta* sched_meta,
                                 const int32_t* num_splits, int num_sm_parts, void* stream) {
   int rc = check_params(p);

@@ -46,4 +46,11 @@ cudaError_t read_kv_write_status(int* flags, cudaStream_t stream);
 cudaError_t launch_div_selftest(const float* scales, int n_scales, unsigned long long* mismatches,
                                 cudaStream_t stream);
 
+// Indexer logits (csrc/mqa_logits.cu).
+constexpr int kMaxMqaRequests = 16384;
+cudaError_t launch_mqa_metadata(const int32_t* ctx, int b, int num_sms, int32_t* sched, cudaStream_t stream);
+cudaError_t launch_mqa_logits(const dsv4b_mqa_logits_params& p, const int32_t* sched, int num_sms,
+                              cudaStream_t stream, int* bad_arg);
+cudaError_t read_mqa_status(int* flags, cudaStream_t stream);
+
 }  // namespace dsv4b

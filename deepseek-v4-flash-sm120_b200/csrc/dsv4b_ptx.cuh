@@ -275,6 +275,43 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
          | ((uint32_t)(M >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor for kind::f8f6f4: e4m3 A/B, fp32 D.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4)                        // D format: F32
+         | (0u << 7)                      // A format: E4M3
+         | (0u << 10)                     // B format: E4M3
+         | ((uint32_t)(N >> 3) << 17)     // N / 8 (A and B K-major)
+         | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f8f6f4 (8-bit inputs, fp32 accumulate).
+__device__ __forceinline__ void umma_f8_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// TMA tiled loads (no multicast) into this CTA's shared memory; the
+// tensor map is a __grid_constant__ kernel parameter.
+__device__ __forceinline__ void tma_load_2d(uint32_t saddr, const void* tmap, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          saddr),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t saddr, const void* tmap, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(saddr),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ------------------------------------------------------------- memory
 #ifndef DSV4B_LDG_QUAL
 #define DSV4B_LDG_QUAL "ld.global.L1::no_allocate"

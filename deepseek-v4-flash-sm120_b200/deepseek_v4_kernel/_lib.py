@@ -33,6 +33,7 @@ EXPORTED = (
     "dsv4b_gather_dequant", "dsv4b_read_kernel_status", "dsv4b_sparse_decode_noalloc",
     "dsv4b_plan_cluster_size", "dsv4b_kv_cache_write",
     "dsv4b_kv_cache_write_status", "dsv4b_kv_write_selftest",
+    "dsv4b_mqa_logits_metadata", "dsv4b_fp8_paged_mqa_logits", "dsv4b_mqa_logits_status",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -93,6 +94,9 @@ def _load():
                                          _i64, _i64, _vp, ctypes.c_int, _vp, _vp]
     lib.dsv4b_kv_cache_write.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp, ctypes.c_int, _i64,
                                          _vp, ctypes.c_int, ctypes.c_int, _i64, _i64, _vp]
+    lib.dsv4b_mqa_logits_metadata.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]
+    lib.dsv4b_fp8_paged_mqa_logits.argtypes = [_vp, _vp, ctypes.c_int, _vp]
+    lib.dsv4b_mqa_logits_status.argtypes = [ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_kv_write_selftest.argtypes = [_vp, ctypes.c_int, _vp, _vp]
     lib.dsv4b_kv_cache_write_status.argtypes = [ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]

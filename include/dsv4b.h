@@ -222,6 +222,54 @@ DSV4B_API int dsv4b_kv_cache_write_status(int* flags, void* stream);
 DSV4B_API int dsv4b_kv_write_selftest(const float* scales, int n_scales,
                                       unsigned long long* mismatches, void* stream);
 
+/* ---------------------------------------------------------------------
+ * Indexer logits (the step that produces `indices`): fp8_paged_mqa_logits.
+ *
+ * For every query row (b, i), i < next_n, and every cache position t:
+ *   logits[b*next_n + i][t] = k_scale[t] *
+ *       sum_h weights[b*next_n + i][h] * relu(sum_d q[b][i][h][d] * k[t][d])
+ * for t < context_lens[b] and t <= context_lens[b] - next_n + i; positions
+ * inside the row's last 128-token tile that fail the test get -inf; with
+ * clean_logits, every later position up to max_model_len gets -inf too.
+ * q and k are e4m3, products are accumulated in fp32 on the tensor cores.
+ * The cache holds, per page, P x d e4m3 values followed by P x fp32 scales
+ * (vLLM's indexer K cache: indexer_k_quant_and_cache).  Same contract as
+ * DeepGEMM's fp8_paged_mqa_logits (vLLM utils/deep_gemm.py:407-460, torch
+ * statement at v1/attention/ops/rocm_aiter_mla_sparse.py:256-300), the
+ * kernel SGLang's DeepSeek-V4 indexer calls on sm_100; the reference only
+ * wraps SGLang's fallbacks (deepseek_v4_kernel/_patch.py:199-236). */
+typedef struct dsv4b_mqa_logits_params {
+  int32_t b, next_n, h, d;        /* d = 128; h in {32, 64, 128}; next_n * h in {32, 64, 128, 256} */
+  const void* q;                  /* e4m3 [b, next_n, h, d], contiguous */
+  const void* kv;                 /* uint8 pages, see above */
+  int32_t num_blocks, page_block_size;  /* P in {32, 64, 128} */
+  int64_t stride_kv_block;        /* bytes between pages (>= P * (d + 4), % 16 == 0) */
+  const float* weights;           /* [b * next_n, h] fp32, contiguous */
+  const int32_t* context_lens;    /* [b] */
+  const int32_t* block_table;     /* [b, >= ceil(context_len / P)] physical page ids */
+  int64_t stride_block_table;     /* elements between rows */
+  float* logits;                  /* [b * next_n, >= max_model_len] fp32 */
+  int64_t stride_logits;          /* elements between rows */
+  int32_t max_model_len;
+  int32_t clean_logits;
+} dsv4b_mqa_logits_params;
+
+/* Schedule for dsv4b_fp8_paged_mqa_logits on num_sms CTAs: writes
+ * sched[num_sms + 1][2] int32 (request, 128-token tile) start positions,
+ * splitting all requests' tiles evenly (on the device, graph capturable).
+ * Mirrors DeepGEMM's get_paged_mqa_logits_metadata (vLLM
+ * utils/deep_gemm.py:386-405).  b <= 16384. */
+DSV4B_API int dsv4b_mqa_logits_metadata(const int32_t* context_lens, int b, int num_sms,
+                                        int32_t* sched, void* stream);
+
+/* The logits kernel (one persistent CTA per schedule entry). */
+DSV4B_API int dsv4b_fp8_paged_mqa_logits(const dsv4b_mqa_logits_params* p, const int32_t* sched,
+                                         int num_sms, void* stream);
+
+/* Reads (and clears) this device's status word of the logits kernel
+ * (0 = no error; 1 = a kernel wait hit its time limit).  Synchronises. */
+DSV4B_API int dsv4b_mqa_logits_status(int* flags, void* stream);
+
 /* Reads (and clears) the kernel status word kept in the workspace into
  * *flags (0 = no error).  Synchronises `stream`. */
 DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
