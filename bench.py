@@ -68,6 +68,8 @@ def parse():
                     help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
                          "logits (fp8_paged_mqa_logits) over config 1's contexts")
     ap.add_argument("--next-n", type=int, default=1, help="mqa_logits: query rows per request")
+    ap.add_argument("--page-order", choices=["random", "sequential"], default="random",
+                    help="mqa_logits: physical order of each request's pages (block table)")
     ap.add_argument("--kv-layout", choices=["v32", "model1"], default="v32")
     ap.add_argument("--tokens", type=int, default=131072, help="kv_write: tokens written per step")
     ap.add_argument("--pages", type=int, default=16384, help="kv_write: cache pages of 256 tokens")
@@ -599,7 +601,10 @@ def run_mqa_logits(args):
     q = torch.randn(B, nn, H, 128, generator=g, device=device).to(torch.float8_e4m3fn)
     w = torch.randn(B * nn, H, generator=g, device=device)
     ctx = torch.full((B,), ctx_len, dtype=torch.int32, device=device)
-    bt = torch.randperm(nb, generator=g, device=device).view(B, pages).int()
+    if args.page_order == "random":
+        bt = torch.randperm(nb, generator=g, device=device).view(B, pages).int()
+    else:
+        bt = torch.arange(nb, device=device, dtype=torch.int32).view(B, pages)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     sched = indexer.get_paged_mqa_logits_metadata(ctx, P, sms)
     out = torch.empty(B * nn, ctx_len, dtype=torch.float32, device=device)
@@ -653,7 +658,7 @@ def run_mqa_logits(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "fp8-e4m3 (fp32 accumulate)",
-        "data": "synthetic (seeded N(0,1) e4m3 q and cache, uniform scales, random page tables)",
+        "data": "synthetic (seeded N(0,1) e4m3 q and cache, uniform scales, %s page tables)" % args.page_order,
         "config": {"workload": f"mqa_logits: b{B} next_n{nn} h{H} d128 ctx{ctx_len} page{P} (config 1 contexts)",
                    "l2": f"no flush: {alg / 1e6:.0f} MB per step, above L2 size"},
         "timing": "one CUDA graph of `steps` launches, CUDA events around its replay",

@@ -15,19 +15,28 @@
 // (M = positions, N = next_n * h query heads, K = d) and an epilogue that
 // reduces the N accumulators of each position to next_n logits.  It is
 // HBM-bound (132 B per position against 2 * N * 128 FLOPs):
-//   * persistent grid, one 256-thread CTA per SM; the tiles of all
+//   * persistent grid, one 384-thread CTA per SM; the tiles of all
 //     requests are split evenly over the CTAs by a device-side schedule
 //     (mqa_meta_kernel, DeepGEMM's get_paged_mqa_logits_metadata);
-//   * warp 0 / lane 0 streams pages with TMA tiled loads (3-D tensor map
-//     over [pages][P][128 B], SWIZZLE_128B, straight into the UMMA K-major
-//     layout) into an 8-stage ring, and each request's Q block (2-D map)
-//     into one of two Q buffers;
-//   * warp 1 / lane 0 issues the four K = 32 kind::f8f6f4 MMAs of a tile
-//     into one of two TMEM accumulators (2 x N columns) and commits them
-//     to the ring slot and the accumulator;
-//   * warps 4-7 (TMEM lanes 0-127 = the tile's positions) read the
-//     accumulator, apply relu, the head weights and the page scale, and
-//     store the logits (consecutive threads, consecutive positions).
+//   * warp 2 reads the block table ahead, 32 entries per parallel batch,
+//     into a double buffer in shared memory;
+//   * warp 0 streams pages with TMA tiled loads (3-D tensor map over
+//     [pages][P][128 B], SWIZZLE_128B, straight into the UMMA K-major
+//     layout) into an 8-stage ring, four tiles per step with one page per
+//     lane (a single issuing thread capped the stream near 3 TB/s);
+//   * warp 1 / lane 0 loads each request's Q block (2-D map, one request
+//     ahead into the other of two buffers) and issues the four K = 32
+//     kind::f8f6f4 MMAs of a tile into one of two TMEM accumulators
+//     (2 x N columns), committing them to the ring slot and the
+//     accumulator;
+//     The producer also bulk-copies each page's scale section into the
+//     stage, so the epilogue never waits on a dependent global load;
+//   * two epilogue groups, warps 4-7 and 8-11 (TMEM lanes 0-127 = the
+//     tile's positions), take alternate tiles (and so one accumulator
+//     each): they read the accumulator, apply relu, the head weights
+//     (staged in shared memory once per request) and the page scale,
+//     release the stage, and store the logits (consecutive threads,
+//     consecutive positions).
 // All waits are bounded (status word g_mqa_status); no multicast.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -48,8 +57,9 @@ namespace {
 constexpr int kTileTok = 128;
 constexpr int kDim = 128;
 constexpr int kStages = 8;
-constexpr int kMqaThreads = 256;
+constexpr int kMqaThreads = 384;  // producer, MMA, 2 idle, two 4-warp epilogue groups
 constexpr int kStageBytes = kTileTok * kDim;  // 16 KB of e4m3
+constexpr int kScaleBytes = kTileTok * 4;     // the tile's page scales
 constexpr int kMetaThreads = 1024;
 
 struct MqaArgs {
@@ -72,14 +82,35 @@ __device__ __forceinline__ int tiles_of(const int32_t* ctx, int b) {
   return c > 0 ? (c + kTileTok - 1) / kTileTok : 0;
 }
 
-// Next (request, tile) in the flattened order, skipping empty requests.
-__device__ __forceinline__ void advance(int& b, int& j, const int32_t* ctx, int B) {
-  if (++j < tiles_of(ctx, b)) return;
-  j = 0;
-  do {
-    ++b;
-  } while (b < B && tiles_of(ctx, b) == 0);
-}
+// A walk over one CTA's tiles that keeps the current request's context
+// length in registers: a global load only when the request changes (a
+// reload per tile put a dependent load latency on every producer step).
+struct TileCursor {
+  const int32_t* ctx_lens;
+  int B, b, j, ctx, tiles, b_end, j_end;
+  __device__ __forceinline__ void load_req() {
+    ctx = b < B ? __ldg(ctx_lens + b) : 0;
+    tiles = ctx > 0 ? (ctx + kTileTok - 1) / kTileTok : 0;
+  }
+  __device__ __forceinline__ void init(const int32_t* c, int nb, int b0, int j0, int b1, int j1) {
+    ctx_lens = c;
+    B = nb;
+    b = b0;
+    j = j0;
+    b_end = b1;
+    j_end = j1;
+    load_req();
+  }
+  __device__ __forceinline__ bool valid() const { return b < B && (b < b_end || (b == b_end && j < j_end)); }
+  __device__ __forceinline__ void next() {
+    if (++j < tiles) return;
+    j = 0;
+    do {
+      ++b;
+      load_req();
+    } while (b < B && tiles == 0);
+  }
+};
 
 // ------------------------------------------------------------------ schedule
 // sched[i] = first (request, tile) of CTA i, sched[G] = (B, 0): CTA i owns
@@ -138,7 +169,9 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t ring = smem_u32(smem);
   const uint32_t qbuf = ring + kStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + 2 * N * kDim);
+  float* scales = reinterpret_cast<float*>(smem + kStages * kStageBytes + 2 * N * kDim);  // [kStages][128]
+  float* wbuf = scales + kStages * kTileTok;                                                 // [2 groups][2][N] head weights
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 4 * N);
   uint64_t* full = bars;
   uint64_t* empty = full + kStages;
   uint64_t* qfull = empty + kStages;
@@ -146,15 +179,18 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
   uint64_t* tfull = qempty + 2;
   uint64_t* tempty = tfull + 2;
   uint64_t* done = tempty + 2;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 1);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+  uint64_t* btfull = done + 1;
+  uint64_t* btempty = btfull + 2;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(btempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(btempty + 3);
+  int* bt_buf = reinterpret_cast<int*>(btempty + 4);  // [2][32] page ids, filled by warp 2
   constexpr uint32_t kTmemCols = 2 * N;  // 64 / 128 / 256 / 512: a power of two
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 1 + 4);  // the MMA commit + one arrive per epilogue warp (after the scales)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qfull[i], 1);
@@ -163,6 +199,10 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
       mbar_init(&tempty[i], 128);
     }
     mbar_init(done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&btfull[i], 1);
+      mbar_init(&btempty[i], 1);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -178,50 +218,115 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
   const int B = a.b;
   const int b0 = sched[2 * blockIdx.x], j0 = sched[2 * blockIdx.x + 1];
   const int b1 = sched[2 * blockIdx.x + 2], j1 = sched[2 * blockIdx.x + 3];
-  auto before_end = [&](int b, int j) { return b < b1 || (b == b1 && j < j1); };
   const int ppt = kTileTok / a.page;  // pages per tile
+  const int tpb = 32 / ppt;           // tiles per 32-entry page-id batch
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
-    int k = 0, rq = -1, prev_b = -1;
-    for (int b = b0, j = j0; b < B && before_end(b, j); advance(b, j, a.ctx, B), ++k) {
-      if (b != prev_b) {
-        ++rq;
-        const int qb = rq & 1;
-        if (rq >= 2 && !mbar_wait(&qempty[qb], ((rq >> 1) - 1) & 1, abort_flag, &g_mqa_status)) break;
-        mbar_arrive_expect_tx(&qfull[qb], N * kDim);
-        tma_load_2d(qbuf + qb * N * kDim, &tmq, 0, b * N, &qfull[qb]);
-        prev_b = b;
+    // One step covers kBatch tiles, one page per lane: lane l takes page
+    // l % ppt of tile k0 + l / ppt.  A single issuing thread needed about
+    // 1,300 SM cycles per tile (cursor, page ids, expect_tx, four copy
+    // issues in sequence), which capped the stream near 3 TB/s; the lanes
+    // issue their copies together.
+    constexpr int kBatch = kStages / 2;
+    const int my_t = lane / ppt, p = lane % ppt;
+    const bool active = my_t < kBatch;
+    TileCursor cur;
+    cur.init(a.ctx, B, b0, j0, b1, j1);
+    for (int i = 0; i < my_t && cur.valid(); ++i) cur.next();
+    int k0 = 0;
+    for (;; k0 += kBatch) {
+      const bool live = active && cur.valid();
+      if (!__any_sync(0xffffffffu, live)) break;
+      const int q = k0 / tpb, slot = q & 1;
+      bool ok = true;
+      if (k0 % tpb == 0) ok = mbar_wait(&btfull[slot], (q >> 1) & 1, abort_flag, &g_mqa_status);
+      const int k = k0 + my_t, s = k % kStages;
+      const bool needed = live && (cur.j * ppt + p) * a.page < cur.ctx;
+      const int phys = needed ? bt_buf[slot * 32 + (k % tpb) * ppt + p] : -1;
+      const bool in_range = needed && phys >= 0 && phys < a.num_blocks;
+      __syncwarp();
+      if ((k0 + kBatch) % tpb == 0 && lane == 0) mbar_arrive(&btempty[slot]);  // the batch is read
+      if (ok && live && p == 0 && k >= kStages)
+        ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, &g_mqa_status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (needed && !in_range)  // an out-of-range page id: values read as zeros (TMA fill), scales 0
+        for (int e = 0; e < a.page; ++e) scales[s * kTileTok + p * a.page + e] = 0.f;
+      const unsigned nmask = __ballot_sync(0xffffffffu, needed);
+      const unsigned vmask = __ballot_sync(0xffffffffu, in_range);
+      __syncwarp();  // the zeroed scales are ordered before the arrive below
+      if (live && p == 0) {
+        const unsigned tile_mask = ((1u << ppt) - 1u) << (my_t * ppt);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(__popc(nmask & tile_mask) * a.page * kDim +
+                                                   __popc(vmask & tile_mask) * a.page * 4));
       }
-      const int s = k % kStages;
-      if (k >= kStages && !mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, &g_mqa_status)) break;
-      const int ctx = __ldg(a.ctx + b);
-      int needed = 0;
-      for (int p = 0; p < ppt; ++p) needed += (j * ppt + p) * a.page < ctx;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(needed * a.page * kDim));
-      const int32_t* bt = a.block_table + (int64_t)b * a.stride_bt;
-      for (int p = 0; p < needed; ++p) {
-        const int phys = __ldg(bt + j * ppt + p);
-        // an out-of-range page id reads zeros (TMA fills outside the map)
-        tma_load_3d(ring + s * kStageBytes + p * a.page * kDim, &tmk, 0, 0, phys, &full[s]);
-      }
+      __syncwarp();
+      if (needed) tma_load_3d(ring + s * kStageBytes + p * a.page * kDim, &tmk, 0, 0, phys, &full[s]);
+      if (in_range)
+        bulk_g2s(smem_u32(scales + s * kTileTok + p * a.page),
+                 a.kv + (int64_t)phys * a.stride_block + (int64_t)a.page * kDim, a.page * 4, &full[s]);
+      for (int i = 0; i < kBatch && cur.valid(); ++i) cur.next();
     }
-    if (*abort_flag) {  // let this CTA's copies land before it exits
-      for (int kk = k - 1; kk >= 0 && kk >= k - kStages; --kk) {
+    if (*abort_flag && lane == 0) {  // let this CTA's copies land before it exits
+      for (int kk = k0 - 1 + kBatch; kk >= 0 && kk >= k0 - kStages; --kk) {
         const long long t0 = clock64();
         while (!mbar_try_wait(smem_u32(&full[kk % kStages]), (kk / kStages) & 1, 1000u) &&
                clock64() - t0 < kWaitLimitCycles) {
         }
       }
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ page ids
+    // Batches of 32 block-table entries (tpb tiles), one per lane, loaded
+    // in parallel into a double buffer ahead of the producer: the
+    // producer's per-tile critical path never waits on a global load.
+    TileCursor cur;  // this lane's cursor: tile q * tpb + lane / ppt
+    cur.init(a.ctx, B, b0, j0, b1, j1);
+    for (int i = 0; i < lane / ppt && cur.valid(); ++i) cur.next();
+    for (int q = 0;; ++q) {
+      const int slot = q & 1;
+      const bool live = cur.valid();
+      if (!__any_sync(0xffffffffu, live)) break;
+      if (q >= 2 && !mbar_wait(&btempty[slot], ((q >> 1) - 1) & 1, abort_flag, &g_mqa_status)) break;
+      int phys = -1;
+      if (live) {
+        const int lp = cur.j * ppt + lane % ppt;
+        if (lp * a.page < cur.ctx) phys = __ldg(a.block_table + (int64_t)cur.b * a.stride_bt + lp);
+      }
+      bt_buf[slot * 32 + lane] = phys;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&btfull[slot]);
+      for (int i = 0; i < tpb && cur.valid(); ++i) cur.next();
+    }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA
     constexpr uint32_t idesc = idesc_e4m3_f32(128, N);
+    // The MMA lane also loads Q: request r goes to buffer r & 1; when r
+    // starts, r + 1's Q is loaded into the other buffer once the MMAs of
+    // r - 1 (its previous user) have completed.
+    auto next_request = [&](int b) {
+      int nb = b + 1;
+      while (nb < B && tiles_of(a.ctx, nb) == 0) ++nb;
+      return (nb < b1 || (nb == b1 && j1 > 0)) ? nb : -1;
+    };
+    auto load_q = [&](int b, int slot) {
+      mbar_arrive_expect_tx(&qfull[slot], N * kDim);
+      tma_load_2d(qbuf + slot * N * kDim, &tmq, 0, b * N, &qfull[slot]);
+    };
     int k = 0, rq = -1, prev_b = -1;
-    for (int b = b0, j = j0; b < B && before_end(b, j); advance(b, j, a.ctx, B), ++k) {
+    TileCursor cur;
+    for (cur.init(a.ctx, B, b0, j0, b1, j1); cur.valid(); cur.next(), ++k) {
+      const int b = cur.b;
       if (b != prev_b) {
-        if (rq >= 0) umma_commit(&qempty[rq & 1]);  // the previous request's Q is free once its MMAs finish
+        if (rq >= 0) umma_commit(&qempty[rq & 1]);  // request rq's Q is free once its MMAs finish
         ++rq;
+        if (rq == 0) load_q(b, 0);
+        const int nb = next_request(b);
+        if (nb >= 0) {
+          const int ns = (rq + 1) & 1;
+          if (rq >= 1 && !mbar_wait(&qempty[ns], ((rq - 1) >> 1) & 1, abort_flag, &g_mqa_status)) break;
+          load_q(nb, ns);
+        }
         if (!mbar_wait(&qfull[rq & 1], (rq >> 1) & 1, abort_flag, &g_mqa_status)) break;
         prev_b = b;
       }
@@ -244,41 +349,62 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int r = (warp - 4) * 32 + lane;  // TMEM lane = position within the tile
+    // Group g (warps 4-7 or 8-11) takes the tiles with k % 2 == g and so
+    // always the same TMEM accumulator.
+    const int g = (warp - 4) >> 2;
+    const int r = ((warp - 4) & 3) * 32 + lane;  // TMEM lane = position within the tile
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int nn = a.next_n, H = a.h;
-    int k = 0;
-    for (int b = b0, j = j0; b < B && before_end(b, j); advance(b, j, a.ctx, B), ++k) {
-      const int acc = k & 1;
-      const int ctx = __ldg(a.ctx + b);
-      const int t = j * kTileTok + r;
-      float scale = 0.f;
-      if (t < ctx) {
-        const int phys = __ldg(a.block_table + (int64_t)b * a.stride_bt + t / a.page);
-        if (phys >= 0 && phys < a.num_blocks)
-          scale = __ldg(reinterpret_cast<const float*>(a.kv + (int64_t)phys * a.stride_block +
-                                                       (int64_t)a.page * kDim) + t % a.page);
+    int k = 0, rq = -1, prev_b = -1;
+    TileCursor cur;
+    for (cur.init(a.ctx, B, b0, j0, b1, j1); cur.valid(); cur.next(), ++k) {
+      if ((k & 1) != g) continue;
+      const int b = cur.b, j = cur.j;
+      const int acc = g, s = k % kStages;
+      if (b != prev_b) {  // this request's head weights into shared memory
+        ++rq;
+        prev_b = b;
+        float* wb = wbuf + (g * 2 + (rq & 1)) * N;
+        for (int e = r; e < N; e += 128) wb[e] = __ldg(a.weights + (int64_t)b * N + e);
+        named_bar_sync(1 + g, 128);
       }
+      const float* wb = wbuf + (g * 2 + (rq & 1)) * N;
+      const int ctx = cur.ctx;
+      const int t = j * kTileTok + r;
       if (!mbar_wait(&tfull[acc], (k >> 1) & 1, abort_flag, &g_mqa_status)) break;
       tc_fence_after();
+      // the stage's phase is complete already (the MMAs consumed it); waiting
+      // on it acquires the bulk-copied scales for this thread.  The stage
+      // cannot move on before this warp's arrive below.
+      if (!mbar_wait(&full[s], (k / kStages) & 1, abort_flag, &g_mqa_status)) break;
+      const float scale = scales[s * kTileTok + r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
       float res[N / 32];  // next_n <= N / 32
       for (int i = 0; i < nn; ++i) {
-        const float4* w = reinterpret_cast<const float4*>(a.weights + ((int64_t)b * nn + i) * H);
-        float sum = 0.f;
-        for (int c = 0; c < H / 32; ++c) {
-          float v[32];
-          tmem_ld32(tmem + lane_base + acc * N + i * H + 32 * c, v);
+        const float4* w = reinterpret_cast<const float4*>(wb + i * H);
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        for (int c = 0; c < H / 32; c += 2) {
+          float v[64];
+          if (c + 1 < H / 32) {
+            tmem_ld64(tmem + lane_base + acc * N + i * H + 32 * c, v);
+          } else {
+            tmem_ld32(tmem + lane_base + acc * N + i * H + 32 * c, *reinterpret_cast<float(*)[32]>(&v[0]));
+          }
           tc_wait_ld();
+          const int ne = c + 1 < H / 32 ? 64 : 32;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const float4 wv = __ldg(w + (32 * c + e) / 4);
-            sum = fmaf(fmaxf(v[e], 0.f), wv.x, sum);
-            sum = fmaf(fmaxf(v[e + 1], 0.f), wv.y, sum);
-            sum = fmaf(fmaxf(v[e + 2], 0.f), wv.z, sum);
-            sum = fmaf(fmaxf(v[e + 3], 0.f), wv.w, sum);
+          for (int e = 0; e < 64; e += 4) {
+            if (e < ne) {
+              const float4 wv = w[(32 * c + e) / 4];
+              s0 = fmaf(fmaxf(v[e], 0.f), wv.x, s0);
+              s1 = fmaf(fmaxf(v[e + 1], 0.f), wv.y, s1);
+              s2 = fmaf(fmaxf(v[e + 2], 0.f), wv.z, s2);
+              s3 = fmaf(fmaxf(v[e + 3], 0.f), wv.w, s3);
+            }
           }
         }
-        res[i] = sum * scale;
+        res[i] = ((s0 + s1) + (s2 + s3)) * scale;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -289,7 +415,7 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
         }
       }
     }
-    if (a.clean && !*abort_flag) {
+    if (a.clean && !*abort_flag && g == 0) {
       // positions past each request's last tile: -inf (requests split over CTAs round-robin)
       for (int b = blockIdx.x; b < B; b += gridDim.x) {
         const int from = tiles_of(a.ctx, b) * kTileTok;
@@ -324,7 +450,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int N>
 cudaError_t launch_logits(const CUtensorMap& tmq, const CUtensorMap& tmk, const MqaArgs& a, const int32_t* sched,
                           int grid, cudaStream_t stream) {
-  constexpr int smem = 1024 + kStages * kStageBytes + 2 * N * kDim + 256;
+  constexpr int smem = 1024 + kStages * kStageBytes + 2 * N * kDim + kStages * kScaleBytes + 4 * N * 4 + 512;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
