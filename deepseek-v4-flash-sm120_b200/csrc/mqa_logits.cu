@@ -56,7 +56,6 @@ namespace {
 
 constexpr int kTileTok = 128;
 constexpr int kDim = 128;
-constexpr int kStages = 8;
 constexpr int kMqaThreads = 384;  // producer, MMA, 2 idle, two 4-warp epilogue groups
 constexpr int kStageBytes = kTileTok * kDim;  // 16 KB of e4m3
 constexpr int kScaleBytes = kTileTok * 4;     // the tile's page scales
@@ -162,9 +161,16 @@ __global__ void __launch_bounds__(kMetaThreads) mqa_meta_kernel(const int32_t* _
 
 // ------------------------------------------------------------------ logits
 template <int N>
+struct MqaRing {
+  // ring depth: as many 16 KB stages as fit beside the Q buffers
+  static constexpr int kStages = 8;  // deeper rings (10-12) measured no faster
+};
+
+template <int N>
 __global__ void __launch_bounds__(kMqaThreads, 1)
 mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const MqaArgs a, const int32_t* __restrict__ sched) {
+  constexpr int kStages = MqaRing<N>::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t ring = smem_u32(smem);
@@ -228,7 +234,7 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     // 1,300 SM cycles per tile (cursor, page ids, expect_tx, four copy
     // issues in sequence), which capped the stream near 3 TB/s; the lanes
     // issue their copies together.
-    constexpr int kBatch = kStages / 2;
+    constexpr int kBatch = 4;
     const int my_t = lane / ppt, p = lane % ppt;
     const bool active = my_t < kBatch;
     TileCursor cur;
@@ -450,7 +456,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int N>
 cudaError_t launch_logits(const CUtensorMap& tmq, const CUtensorMap& tmk, const MqaArgs& a, const int32_t* sched,
                           int grid, cudaStream_t stream) {
-  constexpr int smem = 1024 + kStages * kStageBytes + 2 * N * kDim + kStages * kScaleBytes + 4 * N * 4 + 512;
+  constexpr int kStages = MqaRing<N>::kStages;
+  // barriers: 2 per stage + 11, then the abort flag, the TMEM slot and the
+  // [2][32] page-id buffer
+  constexpr int kBarBytes = (2 * kStages + 11) * 8 + 16 + 2 * 32 * 4;
+  constexpr int smem = 1024 + kStages * kStageBytes + 2 * N * kDim + kStages * kScaleBytes + 4 * N * 4 + kBarBytes;
+  static_assert(smem <= 227 * 1024, "logits kernel shared memory");
   static bool attr_done[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
