@@ -361,6 +361,11 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     const int r = ((warp - 4) & 3) * 32 + lane;  // TMEM lane = position within the tile
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int nn = a.next_n, H = a.h;
+    // One query row of 64 heads (the DeepSeek indexer shape): the row's
+    // weights live in registers for the whole request, so the per-tile sum
+    // is register arithmetic only.
+    const bool w_in_regs = N == 64 && nn == 1;
+    float wr[N == 64 ? 64 : 1];
     int k = 0, rq = -1, prev_b = -1;
     TileCursor cur;
     for (cur.init(a.ctx, B, b0, j0, b1, j1); cur.valid(); cur.next(), ++k) {
@@ -373,6 +378,18 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
         float* wb = wbuf + (g * 2 + (rq & 1)) * N;
         for (int e = r; e < N; e += 128) wb[e] = __ldg(a.weights + (int64_t)b * N + e);
         named_bar_sync(1 + g, 128);
+        if constexpr (N == 64) {
+          if (w_in_regs) {
+#pragma unroll
+            for (int e = 0; e < 64; e += 4) {
+              const float4 wv = reinterpret_cast<const float4*>(wb)[e / 4];
+              wr[e] = wv.x;
+              wr[e + 1] = wv.y;
+              wr[e + 2] = wv.z;
+              wr[e + 3] = wv.w;
+            }
+          }
+        }
       }
       const float* wb = wbuf + (g * 2 + (rq & 1)) * N;
       const int ctx = cur.ctx;
@@ -387,7 +404,25 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       float res[N / 32];  // next_n <= N / 32
-      for (int i = 0; i < nn; ++i) {
+      bool done_sum = false;
+      if constexpr (N == 64) {
+        if (w_in_regs) {
+          float v[64];
+          tmem_ld64(tmem + lane_base + acc * N, v);
+          tc_wait_ld();
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 64; e += 4) {
+            s0 = fmaf(fmaxf(v[e], 0.f), wr[e], s0);
+            s1 = fmaf(fmaxf(v[e + 1], 0.f), wr[e + 1], s1);
+            s2 = fmaf(fmaxf(v[e + 2], 0.f), wr[e + 2], s2);
+            s3 = fmaf(fmaxf(v[e + 3], 0.f), wr[e + 3], s3);
+          }
+          res[0] = ((s0 + s1) + (s2 + s3)) * scale;
+          done_sum = true;
+        }
+      }
+      for (int i = 0; i < nn && !done_sum; ++i) {
         const float4* w = reinterpret_cast<const float4*>(wb + i * H);
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
         for (int c = 0; c < H / 32; c += 2) {
