@@ -28,6 +28,28 @@ BYTES_MODEL1 = 584
 
 _ws_lock = threading.Lock()
 _ws_cache: dict = {}
+# LSE convention, read once at import: DSV4B_LSE_EXCLUDES_SINK=1 returns the
+# FlashMLA-documented LSE without the sink term.
+_LSE_INCLUDES_SINK = os.environ.get("DSV4B_LSE_EXCLUDES_SINK", "0") != "1"
+
+
+class _on_device:
+    """``torch.cuda.device(device)`` only when ``device`` is not already the
+    current device (entering the context costs a few microseconds per call)."""
+
+    __slots__ = ("ctx",)
+
+    def __init__(self, device: torch.device):
+        self.ctx = None if device.index == torch.cuda.current_device() else torch.cuda.device(device)
+
+    def __enter__(self):
+        if self.ctx is not None:
+            self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            return self.ctx.__exit__(*exc)
+        return False
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -43,6 +65,9 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     demand and zero-initialised once.  Calls on one device share it, so
     they must be stream-ordered (the normal case: one decode stream)."""
     key = device.index
+    ws = _ws_cache.get(key)
+    if ws is not None and ws.numel() >= nbytes:  # fast path: no lock
+        return ws
     with _ws_lock:
         ws = _ws_cache.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -200,7 +225,7 @@ def sparse_decode_fwd(
     with the same shapes and the same topk_length / extra_topk_length
     values (FlashMLA's contract, flash_mla_interface.py:83)."""
     if lse_includes_sink is None:
-        lse_includes_sink = os.environ.get("DSV4B_LSE_EXCLUDES_SINK", "0") != "1"
+        lse_includes_sink = _LSE_INCLUDES_SINK
     device = q.device
     b, s_q, h_q, _ = q.shape
     if out is None:
@@ -211,7 +236,7 @@ def sparse_decode_fwd(
     lse = torch.empty((b, h_q, s_q), dtype=torch.float32, device=device)
     p = build_params(q, kv, indices, topk_length, attn_sink, extra_kv, extra_indices,
                      extra_topk_length, d_v, sm_scale, out, lse, lse_includes_sink)
-    with torch.cuda.device(device):
+    with _on_device(device):
         if tile_scheduler_metadata is None or num_splits is None:
             tile_scheduler_metadata, num_splits = get_mla_metadata_tensors(p, device)
         parts = tile_scheduler_metadata.size(0)
