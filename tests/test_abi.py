@@ -76,3 +76,65 @@ def test_ctypes_layout_matches_c_header():
     assert int(got["sizeof_meta"]) == ctypes.sizeof(_lib.SchedMeta) == 32
     for n, _ in _lib.DecodeParams._fields_:
         assert int(got[n]) == getattr(_lib.DecodeParams, n).offset, n
+
+
+def test_mqa_params_layout_matches_c_header():
+    from deepseek_v4_kernel import indexer
+    import ctypes
+    fields = "".join(f"F(dsv4b_mqa_logits_params, {n})" for n, _ in indexer.MqaLogitsParams._fields_)
+    probe = PROBE.replace('printf("sizeof_params %zu\\nsizeof_meta %zu\\n", sizeof(dsv4b_decode_params), '
+                          'sizeof(dsv4b_sched_meta));',
+                          'printf("sizeof_params %zu\\n", sizeof(dsv4b_mqa_logits_params));')
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "probe.c")
+        exe = os.path.join(d, "probe")
+        open(src, "w").write(probe.replace("%FIELDS%", fields))
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), src, "-o", exe], check=True)
+        lines = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = dict(l.split() for l in lines if l.strip())
+    assert int(got["sizeof_params"]) == ctypes.sizeof(indexer.MqaLogitsParams)
+    for n, _ in indexer.MqaLogitsParams._fields_:
+        assert int(got[n]) == getattr(indexer.MqaLogitsParams, n).offset, n
+
+
+def test_writer_and_indexer_reject_bad_arguments_without_a_gpu():
+    """Argument checks run before any CUDA call: these return
+    DSV4B_ERR_INVALID_ARGUMENT (-1) / DSV4B_ERR_UNSUPPORTED (-2) here."""
+    import ctypes
+    from deepseek_v4_kernel import _lib, indexer
+    lib = _lib.lib
+    buf = ctypes.create_string_buffer(1 << 16)
+    a = (ctypes.addressof(buf) + 15) & ~15          # a 16-byte aligned host address (never dereferenced)
+    # writer: bad layout, null cache, misaligned stride, bad slot width, negative n
+    assert lib.dsv4b_kv_cache_write(5, a, 512, a, 64, a, 8, 1, a, 1, 64, 64 * 656, 656, None) == -1
+    assert lib.dsv4b_kv_cache_write(0, a, 512, a, 64, a, 8, 1, None, 1, 64, 64 * 656, 656, None) == -1
+    assert lib.dsv4b_kv_cache_write(0, a, 512, a, 64, a, 8, 1, a, 1, 64, 64 * 656 + 8, 656, None) == -1
+    assert lib.dsv4b_kv_cache_write(0, a, 512, a, 64, a, 2, 1, a, 1, 64, 64 * 656, 656, None) == -1
+    assert lib.dsv4b_kv_cache_write(0, a, 512, a, 64, a, 8, -1, a, 1, 64, 64 * 656, 656, None) == -1
+    assert lib.dsv4b_kv_cache_write(1, a, 512, a + 2, 512, a, 8, 4, a, 1, 64, 64 * 584, 0, None) == -1  # rope misaligned
+    assert lib.dsv4b_kv_cache_write(0, a, 500, a, 64, a, 8, 4, a, 1, 64, 64 * 656, 656, None) == -1    # stride % 8
+    assert lib.dsv4b_kv_cache_write(0, a, 512, a, 64, a, 8, 0, a, 1, 64, 64 * 656, 656, None) == 0     # n = 0: nothing to do
+    flags = ctypes.c_int()
+    assert lib.dsv4b_kv_cache_write_status(None, None) == -1
+    assert lib.dsv4b_kv_write_selftest(None, 1, a, None) == -1
+    # indexer
+    assert lib.dsv4b_mqa_logits_metadata(None, 4, 148, a, None) == -1
+    assert lib.dsv4b_mqa_logits_metadata(a, 0, 148, a, None) == -1
+    assert lib.dsv4b_mqa_logits_metadata(a, 4, 0, a, None) == -1
+    assert lib.dsv4b_mqa_logits_metadata(a, 20000, 148, a, None) == -1
+
+    def params(**kw):
+        p = indexer.MqaLogitsParams(4, 1, 64, 128, a, a, 8, 64, 64 * 132, a, a, a, 4, a, 1024, 1024, 1)
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return p
+
+    ok = params()
+    for bad, rc in ((params(d=64), -1), (params(h=48), -2), (params(next_n=8), -2), (params(page_block_size=48), -2),
+                    (params(stride_kv_block=64 * 132 + 8), -1), (params(stride_kv_block=64 * 100), -1),
+                    (params(q=a + 4), -1), (params(logits=None), -1), (params(stride_logits=100), -1),
+                    (params(b=0), -1)):
+        assert lib.dsv4b_fp8_paged_mqa_logits(ctypes.byref(bad), a, 148, None) == rc
+    assert lib.dsv4b_fp8_paged_mqa_logits(ctypes.byref(ok), None, 148, None) == -1
+    assert lib.dsv4b_fp8_paged_mqa_logits(ctypes.byref(ok), a, 0, None) == -1
+    assert lib.dsv4b_mqa_logits_status(None, None) == -1
