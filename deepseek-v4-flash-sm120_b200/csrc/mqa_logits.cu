@@ -492,9 +492,9 @@ template <int N>
 cudaError_t launch_logits(const CUtensorMap& tmq, const CUtensorMap& tmk, const MqaArgs& a, const int32_t* sched,
                           int grid, cudaStream_t stream) {
   constexpr int kStages = MqaRing<N>::kStages;
-  // then the abort flag, the TMEM slot and the [2][32] page-id buffer
-  // full/empty per stage; qfull, qempty, tfull, tempty, btfull, btempty (2
-  // each); done
+  // mbarriers: full/empty per stage; qfull, qempty, tfull, tempty, btfull,
+  // btempty (2 each); done.  Then the abort flag, the TMEM slot and the
+  // [2][32] page-id buffer.
   constexpr int kNumBars = 2 * kStages + 6 * 2 + 1;
   constexpr int kBarBytes = kNumBars * 8 + 16 + 2 * 32 * 4;
   constexpr int smem = 1024 + kStages * kStageBytes + 2 * N * kDim + kStages * kScaleBytes + 4 * N * 4 + kBarBytes;
