@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kSchedThreads)
 // The decode kernel leaves split partials o_accum[split][h_q][512] (already
 // divided by the split's own row sum) and lse_accum[split][h_q].
 constexpr int kCombineThreads = kDv / 4;  // 128
-constexpr int kCombineMaxSplits = 32;       // splits held in registers; more loop
+constexpr int kCombineRegSplits = 16;       // splits held in registers; more loop
 
 // Launched (outside CUDA-graph capture) as a programmatic dependent of the
 // decode kernel: the CTAs start while the decode grid drains and wait here
@@ -261,43 +261,46 @@ __global__ void __launch_bounds__(kCombineThreads)
   const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)s0 * p.h_q + head) * kDv) + t;
   const int64_t step = (int64_t)p.h_q * (kDv / 4);  // float4s between splits
 
-  // Split LSEs (log2 units) and partial rows, all loads issued up front.
-  float l2[kCombineMaxSplits];
+  // The first kCombineRegSplits partial rows and all their LSEs are loaded
+  // before any arithmetic, so the kernel waits on memory once (the weights
+  // depend on the LSEs, the loads of the rows do not); more splits loop.
+  float4 v[kCombineRegSplits];
+  float l2[kCombineRegSplits];
+#pragma unroll
+  for (int i = 0; i < kCombineRegSplits; ++i) {
+    v[i] = i < n ? __ldg(src + i * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+    l2[i] = i < n ? __ldg(lse_col + (int64_t)i * p.h_q) * kLog2e : -INFINITY;
+  }
   float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kCombineMaxSplits; ++i) {
-    l2[i] = i < n ? __ldg(lse_col + (int64_t)i * p.h_q) * kLog2e : -INFINITY;
-    mx = fmaxf(mx, l2[i]);
-  }
+  for (int i = 0; i < kCombineRegSplits; ++i) mx = fmaxf(mx, l2[i]);
+  for (int i = kCombineRegSplits; i < n; ++i) mx = fmaxf(mx, __ldg(lse_col + (int64_t)i * p.h_q) * kLog2e);
   float sum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kCombineMaxSplits; ++i) {
+  for (int i = 0; i < kCombineRegSplits; ++i) {
     l2[i] = i < n ? exp2f(l2[i] - mx) : 0.0f;
     sum += l2[i];
   }
-  for (int i = kCombineMaxSplits; i < n; ++i) sum += exp2f(__ldg(lse_col + (int64_t)i * p.h_q) * kLog2e - mx);
+  for (int i = kCombineRegSplits; i < n; ++i) sum += exp2f(__ldg(lse_col + (int64_t)i * p.h_q) * kLog2e - mx);
   const float inv = 1.0f / sum;
   const float lse = (mx + log2f(sum)) / kLog2e;
 
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int i = 0; i < kCombineMaxSplits; ++i) {
-    if (i < n) {
-      const float4 v = __ldg(src + i * step);
-      const float wi = l2[i] * inv;
-      acc.x = fmaf(wi, v.x, acc.x);
-      acc.y = fmaf(wi, v.y, acc.y);
-      acc.z = fmaf(wi, v.z, acc.z);
-      acc.w = fmaf(wi, v.w, acc.w);
-    }
+  for (int i = 0; i < kCombineRegSplits; ++i) {
+    const float wi = l2[i] * inv;  // 0 past n
+    acc.x = fmaf(wi, v[i].x, acc.x);
+    acc.y = fmaf(wi, v[i].y, acc.y);
+    acc.z = fmaf(wi, v[i].z, acc.z);
+    acc.w = fmaf(wi, v[i].w, acc.w);
   }
-  for (int i = kCombineMaxSplits; i < n; ++i) {
-    const float4 v = __ldg(src + i * step);
+  for (int i = kCombineRegSplits; i < n; ++i) {
+    const float4 vi = __ldg(src + i * step);
     const float wi = exp2f(__ldg(lse_col + (int64_t)i * p.h_q) * kLog2e - mx) * inv;
-    acc.x = fmaf(wi, v.x, acc.x);
-    acc.y = fmaf(wi, v.y, acc.y);
-    acc.z = fmaf(wi, v.z, acc.z);
-    acc.w = fmaf(wi, v.w, acc.w);
+    acc.x = fmaf(wi, vi.x, acc.x);
+    acc.y = fmaf(wi, vi.y, acc.y);
+    acc.z = fmaf(wi, vi.z, acc.z);
+    acc.w = fmaf(wi, vi.w, acc.w);
   }
   float scale = 1.0f, lse_out = lse;
   if (p.attn_sink) {
