@@ -63,6 +63,8 @@ def parse():
                          "(b, h_q, top-k) on a smaller cache, for profiler captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-next-rows", action="store_true",
+                    help="skip the writer / indexer summaries in the config-1 line")
     ap.add_argument("--json-out", default=None)
     ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits"], default="decode",
                     help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
@@ -470,10 +472,39 @@ def run_ours(args, spec, world, rank, local_rank):
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_quick(spec, bt)
+    if world == 1 and args.config == 1 and not args.no_next_rows:
+        line["next_rows"] = next_rows(args)
     print(json.dumps(line), flush=True)
     if args.json_out:
         with open(args.json_out, "w") as f:
             f.write(json.dumps(line) + "\n")
+
+
+def next_rows(args):
+    """The two steps either side of the decode (SURVEY next rows), measured
+    with their own bench modes and summarised in the headline line: the
+    KV-cache writer (131,072 tokens, V32 and MODEL1) and the indexer logits
+    (config 1's contexts).  A failure here is reported, not raised."""
+    import copy
+    import torch
+    out = {}
+    for name, fn, kw in (("kv_write_v32", run_kv_write, {"kv_layout": "v32"}),
+                         ("kv_write_model1", run_kv_write, {"kv_layout": "model1"}),
+                         ("mqa_logits", run_mqa_logits, {})):
+        a = copy.copy(args)
+        a.steps, a.warmup, a.tokens, a.pages, a.slots = 20, 3, 131072, 16384, "paged"
+        a.next_n, a.page_order, a.batch, a.ctx = 1, "random", None, None
+        for k, v in kw.items():
+            setattr(a, k, v)
+        try:
+            d = fn(a)
+            out[name] = {"metric": d["metric"], "value": d["value"], "unit": d["unit"],
+                         "workload": d["config"]["workload"], "roofline": d["roofline"],
+                         "cpu_baseline": d["cpu_baseline"], "gpu_launches": d["gpu_launches"]}
+        except Exception as e:  # reported in the line, the headline stands
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_kv_write(args):
@@ -582,10 +613,7 @@ def run_kv_write(args):
                          "kind": "port", "sample": f"oracle/kv_writer_oracle.py on {sample} of the {n} "
                                                    f"tokens, scaled to {n}"},
     }
-    print(json.dumps(line), flush=True)
-    if args.json_out:
-        with open(args.json_out, "w") as f:
-            f.write(json.dumps(line) + "\n")
+    return line
 
 
 def run_mqa_logits(args):
@@ -686,10 +714,7 @@ def run_mqa_logits(args):
                          "sample": f"oracle/mqa_logits_oracle.py (float64 numpy) on 1 of the {B} requests, "
                                    f"scaled to {B}"},
     }
-    print(json.dumps(line), flush=True)
-    if args.json_out:
-        with open(args.json_out, "w") as f:
-            f.write(json.dumps(line) + "\n")
+    return line
 
 
 def run_sweep(args):
@@ -789,7 +814,11 @@ def main():
     args = parse()
     if args.op in ("kv_write", "mqa_logits"):
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            (run_kv_write if args.op == "kv_write" else run_mqa_logits)(args)
+            line = (run_kv_write if args.op == "kv_write" else run_mqa_logits)(args)
+            print(json.dumps(line), flush=True)
+            if args.json_out:
+                with open(args.json_out, "w") as f:
+                    f.write(json.dumps(line) + "\n")
         return
     if args.config == 3 and args.impl == "ours":
         run_sweep(args)
