@@ -144,6 +144,31 @@ class ClockSampler:
         }
 
 
+def bind_to_gpu_numa_node(device_index: int):
+    """Pin this process's CPU affinity to the NUMA node of the GPU's PCIe
+    root before pinned host buffers are allocated, so that host <-> device
+    copies do not cross sockets.  Returns the node, or None where the
+    topology is not visible (nothing is changed then)."""
+    try:
+        import torch
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:
+        return None
+
+
 # ------------------------------------------------------------------ workload
 def workload(cfg: int, batch_override, rank: int, ctx_override=None):
     from deepseek_v4_kernel import kvcache
@@ -373,6 +398,7 @@ def run_ours(args, spec, world, rank, local_rank):
     # e2e through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        numa_node = bind_to_gpu_numa_node(local_rank)
         q_host = q.cpu().pin_memory()
         idx_host = bt.indices.cpu().pin_memory()
         q_dev = torch.empty_like(q)
@@ -411,7 +437,8 @@ def run_ours(args, spec, world, rank, local_rank):
         e2e = {"value": round(t_e2e * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h,
                "path": "deepseek_v4_kernel.flash_mla_with_kvcache (FlashMLASchedMeta reused), "
-                       "pinned host q/indices -> device, out/lse -> pinned host"}
+                       "pinned host q/indices -> device, out/lse -> pinned host",
+               "host_numa_node": numa_node}
 
     if rank != 0:
         return
