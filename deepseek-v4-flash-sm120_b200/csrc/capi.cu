@@ -114,27 +114,23 @@ int check_workspace(const dsv4b_decode_params* p, int parts, void* ws, size_t ws
   return DSV4B_OK;
 }
 
-// Built-in scratch for dsv4b_sparse_decode_noalloc: every GPU that loads the
-// library holds DSV4B_NOALLOC_SCRATCH_BYTES of it until process exit.  In
-// host code the name is only a host-side stand-in; the device address comes
-// from cudaGetSymbolAddress (per device, with that device current).
+// Built-in scratch for dsv4b_sparse_decode_noalloc: a __device__ array of
+// the library's module, so each device holds DSV4B_NOALLOC_SCRATCH_BYTES of
+// it from the moment the module is loaded on that device (with lazy module
+// loading, the CUDA default, that is the first call that touches the
+// module there) until the context is destroyed.  In host code the name is
+// only a host-side stand-in; the device address comes from
+// cudaGetSymbolAddress with the device current.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[DSV4B_NOALLOC_SCRATCH_BYTES];
 
-void* g_noalloc_ptr[64];  // device address of g_noalloc_scratch, per device
-
-// Device address of this device's scratch; looked up once per device (the
-// first call on a device), never allocates.
+// Device address of the current device's scratch.  Looked up on every call
+// (a runtime table lookup, no allocation once the module is loaded): a
+// cached address would go stale when the context is reset and recreated.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return DSV4B_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return DSV4B_ERR_INVALID_ARGUMENT;
-  if (!g_noalloc_ptr[dev]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr) return cuda_rc(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-    g_noalloc_ptr[dev] = ptr;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || !ptr) return cuda_rc(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+  *out = ptr;
   return DSV4B_OK;
 }
 
@@ -356,11 +352,27 @@ int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p, const dsv4b_sched_
                                        reinterpret_cast<const float*>(ws + w.o_off), s));
 }
 
-int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes, int* flags, void* stream) {
-  if (!workspace || workspace_bytes < kStatusBytes || !flags) return DSV4B_ERR_INVALID_ARGUMENT;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = cuda_rc(cudaMemcpyAsync(flags, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
+int dsv4b_set_test_stall(int kernels) {
+  if (kernels & ~(DSV4B_STALL_DECODE | DSV4B_STALL_KV_WRITE | DSV4B_STALL_MQA_LOGITS))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
   if (rc) return rc;
+  if ((rc = cuda_rc(dsv4b::set_decode_test_stall((kernels & DSV4B_STALL_DECODE) != 0)))) return rc;
+  if ((rc = cuda_rc(dsv4b::set_kv_write_test_stall((kernels & DSV4B_STALL_KV_WRITE) != 0)))) return rc;
+  return cuda_rc(dsv4b::set_mqa_test_stall((kernels & DSV4B_STALL_MQA_LOGITS) != 0));
+}
+
+int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes, int* flags, void* stream) {
+  if (!flags) return DSV4B_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (!workspace && workspace_bytes == 0) {  // the status word of dsv4b_sparse_decode_noalloc
+    if ((rc = current_arch_ok())) return rc;
+    if ((rc = noalloc_scratch(&workspace))) return rc;
+    workspace_bytes = kStatusBytes;
+  }
+  if (!workspace || workspace_bytes < kStatusBytes) return DSV4B_ERR_INVALID_ARGUMENT;
+  if ((rc = cuda_rc(cudaMemcpyAsync(flags, workspace, sizeof(int), cudaMemcpyDeviceToHost, s)))) return rc;
   if ((rc = cuda_rc(cudaStreamSynchronize(s)))) return rc;
   return cuda_rc(cudaMemsetAsync(workspace, 0, sizeof(int), s));
 }

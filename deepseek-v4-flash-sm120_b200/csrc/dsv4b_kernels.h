@@ -21,6 +21,10 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
 
 int decode_smem_bytes(int layout);
 
+// Test hook: whether the decode kernel's producers withhold their first
+// Q^T arrival on the current device (stall != 0), so that a wait runs out.
+cudaError_t set_decode_test_stall(int stall);
+
 // Cluster size of the split plan for this batch (1 = no cluster: split
 // partials go through the combine kernel).  The scheduler, the decode
 // launch and the C ABI all decide with this one function.
@@ -43,6 +47,7 @@ cudaError_t launch_kv_cache_write(int layout, const void* nope, int64_t stride_n
                                   int64_t stride_row, cudaStream_t stream);
 
 cudaError_t read_kv_write_status(int* flags, cudaStream_t stream);
+cudaError_t set_kv_write_test_stall(int stall);  // test hook, see dsv4b_set_test_stall
 cudaError_t launch_div_selftest(const float* scales, int n_scales, unsigned long long* mismatches,
                                 cudaStream_t stream);
 
@@ -52,5 +57,6 @@ cudaError_t launch_mqa_metadata(const int32_t* ctx, int b, int num_sms, int32_t*
 cudaError_t launch_mqa_logits(const dsv4b_mqa_logits_params& p, const int32_t* sched, int num_sms,
                               cudaStream_t stream, int* bad_arg);
 cudaError_t read_mqa_status(int* flags, cudaStream_t stream);
+cudaError_t set_mqa_test_stall(int stall);  // test hook, see dsv4b_set_test_stall
 
 }  // namespace dsv4b

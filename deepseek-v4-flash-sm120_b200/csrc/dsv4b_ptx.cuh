@@ -59,18 +59,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and
-// raises the CTA abort flag plus the global error word) once about
-// kWaitLimitCycles SM cycles have passed, or when another role already
-// aborted.
+// raises the CTA abort flag plus the global error word) once about `limit`
+// SM cycles (default kWaitLimitCycles) have passed, or when another role
+// already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* cta_abort, int* err_word) {
+                                          volatile int* cta_abort, int* err_word,
+                                          long long limit = kWaitLimitCycles) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(a, parity)) return true;
     if (*cta_abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       *cta_abort = 1;
       if (err_word) atomicOr(err_word, kErrWaitTimeout);
       return false;

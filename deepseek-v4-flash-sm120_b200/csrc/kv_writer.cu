@@ -55,6 +55,10 @@
 namespace dsv4b {
 
 __device__ int g_kv_write_status;  // kErr* bits of the writer kernels on this device
+// Test hook (dsv4b_set_test_stall): when set, the producer of every CTA
+// skips its first chunk's copies and arrival, so the consumers' first wait
+// runs out.
+__device__ int g_kv_write_test_stall = 0;
 
 namespace {
 
@@ -317,10 +321,12 @@ __global__ void __launch_bounds__(kWriterThreads, 1) kv_write_kernel(const Write
 
   if (warp == kConsumerWarps) {
     // ---------------------------------------------------------- producer
+    const bool withhold_first = g_kv_write_test_stall != 0;
     int k = 0;
     for (int64_t c = blockIdx.x; c < chunks; c += gridDim.x, ++k) {
       const int s = k % kStages;
       if (k >= kStages && !mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, &g_kv_write_status)) break;
+      if (withhold_first && k == 0) continue;
       const int64_t t0 = c * kChunkTok;
       const int ntok = a.n - t0 < kChunkTok ? (int)(a.n - t0) : kChunkTok;
       const uint32_t stage = ring + s * kStageBytes;
@@ -346,6 +352,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1) kv_write_kernel(const Write
     // before the CTA's shared memory goes away.
     if (*abort_flag && lane == 0) {
       for (int j = k - 1; j >= 0 && j >= k - kStages; --j) {
+        if (withhold_first && j == 0) continue;  // nothing was issued for it
         const uint32_t fa = smem_u32(&full[j % kStages]);
         const long long t0 = clock64();
         while (!mbar_try_wait(fa, (j / kStages) & 1, 1000u) && clock64() - t0 < kWaitLimitCycles) {
@@ -479,6 +486,10 @@ cudaError_t launch_div_selftest(const float* scales, int n_scales, unsigned long
                                 cudaStream_t stream) {
   div_selftest_kernel<<<dim3(64, 256), 1024, 0, stream>>>(scales, n_scales, mismatches);
   return cudaGetLastError();
+}
+
+cudaError_t set_kv_write_test_stall(int stall) {
+  return cudaMemcpyToSymbol(g_kv_write_test_stall, &stall, sizeof(stall));
 }
 
 cudaError_t read_kv_write_status(int* flags, cudaStream_t stream) {

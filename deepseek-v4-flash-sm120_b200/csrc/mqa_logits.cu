@@ -51,6 +51,9 @@
 namespace dsv4b {
 
 __device__ int g_mqa_status;  // kErr* bits of the logits kernel on this device
+// Test hook (dsv4b_set_test_stall): when set, the page-id warp of every
+// CTA withholds its first arrival, so the producer's first wait runs out.
+__device__ int g_mqa_test_stall = 0;
 
 namespace {
 
@@ -274,7 +277,9 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
       for (int i = 0; i < kBatch && cur.valid(); ++i) cur.next();
     }
     if (*abort_flag && lane == 0) {  // let this CTA's copies land before it exits
-      for (int kk = k0 - 1 + kBatch; kk >= 0 && kk >= k0 - kStages; --kk) {
+      // Both loop exits come before batch k0's copies are issued: the
+      // stages in flight are those of tiles k0 - kStages .. k0 - 1.
+      for (int kk = k0 - 1; kk >= 0 && kk >= k0 - kStages; --kk) {
         const long long t0 = clock64();
         while (!mbar_try_wait(smem_u32(&full[kk % kStages]), (kk / kStages) & 1, 1000u) &&
                clock64() - t0 < kWaitLimitCycles) {
@@ -286,6 +291,9 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     // Batches of 32 block-table entries (tpb tiles), one per lane, loaded
     // in parallel into a double buffer ahead of the producer: the
     // producer's per-tile critical path never waits on a global load.
+    // Test hook: withhold the first batch's arrival, so the producer's
+    // first wait can only run out.
+    const bool withhold_first = g_mqa_test_stall != 0;
     TileCursor cur;  // this lane's cursor: tile q * tpb + lane / ppt
     cur.init(a.ctx, B, b0, j0, b1, j1);
     for (int i = 0; i < lane / ppt && cur.valid(); ++i) cur.next();
@@ -301,7 +309,7 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
       }
       bt_buf[slot * 32 + lane] = phys;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&btfull[slot]);
+      if (lane == 0 && !(withhold_first && q == 0)) mbar_arrive(&btfull[slot]);
       for (int i = 0; i < tpb && cur.valid(); ++i) cur.next();
     }
   } else if (warp == 1 && lane == 0) {
@@ -315,9 +323,11 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
       while (nb < B && tiles_of(a.ctx, nb) == 0) ++nb;
       return (nb < b1 || (nb == b1 && j1 > 0)) ? nb : -1;
     };
+    int q_loads0 = 0, q_loads1 = 0;  // Q loads issued into buffer 0 / 1 (scalars: no local memory)
     auto load_q = [&](int b, int slot) {
       mbar_arrive_expect_tx(&qfull[slot], N * kDim);
       tma_load_2d(qbuf + slot * N * kDim, &tmq, 0, b * N, &qfull[slot]);
+      if (slot) ++q_loads1; else ++q_loads0;
     };
     int k = 0, rq = -1, prev_b = -1;
     TileCursor cur;
@@ -353,6 +363,18 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     const long long t0 = clock64();
     while (!mbar_try_wait(smem_u32(done), 0, 1000u) && clock64() - t0 < kWaitLimitCycles) {
     }
+    // after an abort, the last Q load of each buffer may still be in
+    // flight: it lands before the CTA's shared memory goes away
+    if (*abort_flag) {
+      for (int i = 0; i < 2; ++i) {
+        const int nq = i ? q_loads1 : q_loads0;
+        if (nq == 0) continue;
+        const long long t1 = clock64();
+        while (!mbar_try_wait(smem_u32(&qfull[i]), (nq - 1) & 1, 1000u) &&
+               clock64() - t1 < kWaitLimitCycles) {
+        }
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     // Group g (warps 4-7 or 8-11) takes the tiles with k % 2 == g and so
@@ -366,6 +388,14 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     // is register arithmetic only.
     const bool w_in_regs = N == 64 && nn == 1;
     float wr[N == 64 ? 64 : 1];
+    // After a failed wait a warp stops working but keeps walking its tiles:
+    // its group's named barrier (at each request change) still counts on
+    // it, and a wait can give up in one warp while the barrier completes
+    // for another, so leaving the loop could strand the group's others.
+    // The lanes of a warp poll their waits in lockstep (nothing before them
+    // diverges), so they give up together; a per-tile warp vote to enforce
+    // that measured 7% slower on B200 at b = 32 x 131,072 positions.
+    bool dead = false;
     int k = 0, rq = -1, prev_b = -1;
     TileCursor cur;
     for (cur.init(a.ctx, B, b0, j0, b1, j1); cur.valid(); cur.next(), ++k) {
@@ -391,15 +421,19 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
           }
         }
       }
+      if (dead) continue;
       const float* wb = wbuf + (g * 2 + (rq & 1)) * N;
       const int ctx = cur.ctx;
       const int t = j * kTileTok + r;
-      if (!mbar_wait(&tfull[acc], (k >> 1) & 1, abort_flag, &g_mqa_status)) break;
+      if (!mbar_wait(&tfull[acc], (k >> 1) & 1, abort_flag, &g_mqa_status)) {
+        dead = true;
+        continue;
+      }
       tc_fence_after();
-      // the stage's phase is complete already (the MMAs consumed it); waiting
-      // on it acquires the bulk-copied scales for this thread.  The stage
-      // cannot move on before this warp's arrive below.
-      if (!mbar_wait(&full[s], (k / kStages) & 1, abort_flag, &g_mqa_status)) break;
+      if (!mbar_wait(&full[s], (k / kStages) & 1, abort_flag, &g_mqa_status)) {
+        dead = true;
+        continue;
+      }
       const float scale = scales[s * kTileTok + r];
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -584,6 +618,10 @@ cudaError_t launch_mqa_logits(const dsv4b_mqa_logits_params& p, const int32_t* s
     case 256: return launch_logits<256>(tmq, tmk, a, sched, num_sms, stream);
     default: *bad_arg = 1; return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t set_mqa_test_stall(int stall) {
+  return cudaMemcpyToSymbol(g_mqa_test_stall, &stall, sizeof(stall));
 }
 
 cudaError_t read_mqa_status(int* flags, cudaStream_t stream) {

@@ -48,6 +48,13 @@
 
 namespace dsv4b {
 
+// Test hook (dsv4b_set_test_stall): when set, producer thread 0 of
+// every CTA withholds its first Q^T arrival, so the MMA issuer's first wait
+// can only run out.  The waits themselves keep the compile-time limit
+// kWaitLimitCycles: reading a limit from device memory inside them, even
+// only on their slow path, measured 2 us slower per decode call on B200.
+__device__ int g_decode_test_stall = 0;
+
 #ifdef DSV4B_TRACE
 // Debug-build phase trace (never in the shipped library).  The recording
 // thread of each role writes (clock64 | event | arg) words with plain
@@ -113,6 +120,7 @@ struct Misc {
   uint64_t full[9];
   uint64_t empty[5];
   uint64_t s_full, p_full, q_full, q_empty, o_full;
+  uint64_t drain;  // end of the MMA issuer's tcgen05 work (abort path)
   uint32_t tmem_base;
   int abort;
   uint32_t sink_word;  // target of the producers' load-completion fold
@@ -316,6 +324,9 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
                   qb + (ok ? (int64_t)head * p.stride_q_h + ch * 64 + u * 8 : 0), ok ? 16u : 0u);
     }
   };
+  // Test hook (read here, off the critical path: the load completes
+  // while the first tile's rows are in flight).
+  const bool withhold_first_q = ptid == 0 && g_decode_test_stall != 0;
   // The first row's Q^T is in flight together with the first tile's loads.
   issue_q(cur);
 
@@ -341,7 +352,7 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
       }
       cp_async_wait_all();
       fence_proxy_async_smem();
-      mbar_arrive(&M.q_full);
+      if (seg_count != 0 || !withhold_first_q) mbar_arrive(&M.q_full);
       if (ptid == 0) DSV4B_TR_ROLE(0, 5, seg_count);
       ++seg_count;
     }
@@ -714,6 +725,18 @@ __device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& 
   if (st < 64) M.red[1][st] = m_run;
 }
 
+// The softmax threads leave on a wait failure only all together: each
+// thread's own bounded wait can give up at a slightly different moment (its
+// time limit, or the CTA abort flag raised by another role, possibly just
+// as the barrier completes), and a thread that went on while another left
+// would wait forever at the group's next named barrier.  group_ok() ORs
+// the failures over named barrier 1 (one vote, every thread gets the same
+// answer).  A failed MMA issuer stops issuing but stays in the group.
+__device__ __forceinline__ bool group_ok(bool ok) {
+  __syncwarp();  // bar.red is warp-aligned: the lanes left their polls at different times
+  return !named_bar_or(1, kSoftmaxThreads, !ok);
+}
+
 template <int L>
 __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
                             const int32_t* num_splits, float* lse_accum, float* o_accum,
@@ -735,19 +758,20 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     M.red[2][st] = 0.0f;
   }
   // MMA issue of the first tile; later tiles' QK^T follows the previous PV.
-  if (q == 0) {
-    bool ok = true;
-    if (mma_lane && cur.valid) ok = mma_qk<L>(cur, ms, q_s, slot_s, tmem, M, err);
-    __syncwarp();
-    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-  }
+  bool mma_ok = true;  // lane 0 of warp kMmaWarp: false once an MMA-side wait gave up
+  if (mma_lane && cur.valid) mma_ok = mma_qk<L>(cur, ms, q_s, slot_s, tmem, M, err);
+  __syncwarp();
   while (cur.valid) {
     const bool seg_first = cur.t == cur.t_lo;
     const bool seg_last = cur.t + 1 == cur.t_hi;
     if (seg_first) m_run = -INFINITY;
     const float row_scale = st < tile_span(p, cur).npos ? scale_log2 : 0.0f;  // 0 marks padding rows
 
-    if (!mbar_wait(&M.s_full, tile_count & 1, abort_flag, err)) return;
+    // On a failed wait the thread still runs this tile's softmax pass on
+    // whatever TMEM holds (harmless) so that the group's vote below, which
+    // the pass needs anyway, also carries the failure: no extra barrier per
+    // tile.
+    const bool s_ok = mbar_wait(&M.s_full, tile_count & 1, abort_flag, err);
     if (st == 0) DSV4B_TR_ROLE(2, 20, tile_count);
     tc_fence_after();
 
@@ -758,11 +782,17 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     // (tcgen05.ld / wait::ld are .sync.aligned: every lane executes them,
     // padding rows included.)
     if (seg_first) {
+      if (!group_ok(s_ok)) return;
       softmax_max_path(tl, row_scale, true, m_run, M);
       softmax_p_pass(tl, row_scale, p_s, M);
-    } else if (named_bar_or(1, kSoftmaxThreads, softmax_p_pass(tl, row_scale, p_s, M))) {
-      softmax_max_path(tl, row_scale, false, m_run, M);
-      softmax_p_pass(tl, row_scale, p_s, M);
+    } else {
+      const bool exceed = softmax_p_pass(tl, row_scale, p_s, M);
+      __syncwarp();
+      if (named_bar_or(1, kSoftmaxThreads, exceed || !s_ok)) {
+        if (!group_ok(s_ok)) return;
+        softmax_max_path(tl, row_scale, false, m_run, M);
+        softmax_p_pass(tl, row_scale, p_s, M);
+      }
     }
     tc_wait_st();
     fence_proxy_async_smem();
@@ -770,20 +800,16 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     mbar_arrive(&M.p_full);
     if (st == 0) DSV4B_TR_ROLE(2, 23, tile_count);
     const TileCursor nxt = cursor_next(p, sm, cur);
-    if (q == 0) {  // the MMA issuer's turn: PV of this tile, QK^T of the next
-      bool ok = true;
-      if (mma_lane) {
-        ok = mma_pv<L>(cur, ms, slot_s, p_s, tmem, M, err);
-        if (cur.t + 1 == cur.t_hi) ++ms.seg_count;
-        ++ms.tile_count;
-        if (ok && nxt.valid) ok = mma_qk<L>(nxt, ms, q_s, slot_s, tmem, M, err);
-      }
-      __syncwarp();
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    if (mma_lane && mma_ok) {  // the MMA issuer's turn: PV of this tile, QK^T of the next
+      mma_ok = mma_pv<L>(cur, ms, slot_s, p_s, tmem, M, err);
+      if (cur.t + 1 == cur.t_hi) ++ms.seg_count;
+      ++ms.tile_count;
+      if (mma_ok && nxt.valid) mma_ok = mma_qk<L>(nxt, ms, q_s, slot_s, tmem, M, err);
     }
+    __syncwarp();
 
     if (seg_last) {
-      if (!mbar_wait(&M.o_full, seg_count & 1, abort_flag, err)) return;
+      if (!group_ok(mbar_wait(&M.o_full, seg_count & 1, abort_flag, err))) return;
       if (st == 0) DSV4B_TR_ROLE(2, 24, seg_count);
       tc_fence_after();
       if (cluster_c > 1) {
@@ -979,6 +1005,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&M.q_full, kProducerThreads);
     mbar_init(&M.q_empty, 1);
     mbar_init(&M.o_full, 1);
+    mbar_init(&M.drain, 1);
     M.abort = 0;
 #ifdef DSV4B_TRACE
     s_trace_n[0] = s_trace_n[1] = s_trace_n[2] = 0;
@@ -1008,8 +1035,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kProducerWarps) {
     run_producer<L>(p, sm, g, q_s, slot_s, M, err);
+    cp_async_wait_all();  // an aborted producer may still have Q^T copies in flight
   } else {
     run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, q_s, slot_s, p_s, tmem, M, err, cluster_c);
+    if (warp == kMmaWarp) {
+      // Every tcgen05.mma the issuer started must be complete before shared
+      // memory is reused by the cluster merge and TMEM is freed.  On the
+      // normal path the last o_full commit already covered them; after an
+      // abort this commit + wait does (a bounded wait that ignores the
+      // abort flag: MMAs always complete, their operands are resident).
+      if (threadIdx.x == kProducerThreads) umma_commit(&M.drain);
+      __syncwarp();
+      const long long t0 = clock64();
+      while (!mbar_try_wait(smem_u32(&M.drain), 0) && clock64() - t0 < kWaitLimitCycles) {
+      }
+    }
   }
 
   tc_fence_before();
@@ -1164,6 +1204,10 @@ extern "C" DSV4B_API int dsv4b_debug_trace_read(unsigned long long* dst, int max
 int decode_smem_bytes(int layout) {
   return layout == DSV4B_LAYOUT_V32 ? SmemPlan<DSV4B_LAYOUT_V32>::kBytes
                                     : SmemPlan<DSV4B_LAYOUT_MODEL1>::kBytes;
+}
+
+cudaError_t set_decode_test_stall(int stall) {
+  return cudaMemcpyToSymbol(g_decode_test_stall, &stall, sizeof(stall));
 }
 
 }  // namespace dsv4b

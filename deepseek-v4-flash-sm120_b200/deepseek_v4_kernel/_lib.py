@@ -34,9 +34,13 @@ EXPORTED = (
     "dsv4b_plan_cluster_size", "dsv4b_kv_cache_write",
     "dsv4b_kv_cache_write_status", "dsv4b_kv_write_selftest",
     "dsv4b_mqa_logits_metadata", "dsv4b_fp8_paged_mqa_logits", "dsv4b_mqa_logits_status",
+    "dsv4b_set_test_stall",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
+
+# dsv4b_set_test_stall bits
+STALL_DECODE, STALL_KV_WRITE, STALL_MQA_LOGITS = 1, 2, 4
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -101,6 +105,7 @@ def _load():
     lib.dsv4b_kv_cache_write_status.argtypes = [ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]
     lib.dsv4b_read_kernel_status.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int), _vp]
+    lib.dsv4b_set_test_stall.argtypes = [ctypes.c_int]
     return lib
 
 

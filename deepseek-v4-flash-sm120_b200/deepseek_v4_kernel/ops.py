@@ -31,6 +31,11 @@ _ws_cache: dict = {}
 # LSE convention, read once at import: DSV4B_LSE_EXCLUDES_SINK=1 returns the
 # FlashMLA-documented LSE without the sink term.
 _LSE_INCLUDES_SINK = os.environ.get("DSV4B_LSE_EXCLUDES_SINK", "0") != "1"
+# DSV4B_CHECK_STATUS=1 (read once at import): sparse_decode_fwd synchronises
+# after each call, reads the kernel status word and raises DSV4BError with
+# DSV4B_ERR_KERNEL_TIMEOUT when a bounded wait ran out (the call's outputs
+# are then invalid).  Off by default: the check costs a device sync.
+CHECK_STATUS = os.environ.get("DSV4B_CHECK_STATUS", "0") == "1"
 
 
 class _on_device:
@@ -249,7 +254,17 @@ def sparse_decode_fwd(
               lib.dsv4b_sparse_decode(ctypes.byref(p), tile_scheduler_metadata.data_ptr(),
                                       num_splits.data_ptr(), parts, ws.data_ptr(), ws.numel(),
                                       _stream(device)))
+        if CHECK_STATUS:
+            _raise_on_status(ws, device)
     return out, lse, tile_scheduler_metadata, num_splits
+
+
+def _raise_on_status(ws: torch.Tensor, device: torch.device) -> None:
+    flags = ctypes.c_int()
+    check("dsv4b_read_kernel_status",
+          lib.dsv4b_read_kernel_status(ws.data_ptr(), ws.numel(), ctypes.byref(flags), _stream(device)))
+    if flags.value:
+        raise _lib.DSV4BError("sparse_decode_fwd (kernel status)", -6)
 
 
 def gather_dequant(kv: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:

@@ -271,12 +271,40 @@ DSV4B_API int dsv4b_fp8_paged_mqa_logits(const dsv4b_mqa_logits_params* p, const
 DSV4B_API int dsv4b_mqa_logits_status(int* flags, void* stream);
 
 /* Reads (and clears) the kernel status word kept in the workspace into
- * *flags (0 = no error).  Synchronises `stream`. */
+ * *flags (0 = no error; bit 0 = a bounded wait ran out of time, the call's
+ * outputs are then invalid).  Synchronises `stream`.  workspace = NULL
+ * with workspace_bytes = 0 reads (and clears) the status word of
+ * dsv4b_sparse_decode_noalloc's built-in scratch on the current device. */
 DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
                              int* flags, void* stream);
 
+/* Test hook for the kernels' failure path, on the current device.  Every
+ * mbarrier wait inside the library's kernels gives up after a time limit
+ * (4e9 SM cycles, about 2 s); the CTA then raises an abort flag, every
+ * role leaves (waiting, bounded, for its own copies and tensor-core work
+ * in flight), TMEM is freed and the kernel's status word gets bit 0.  The
+ * kernel returns normally: no fault, no hang, the context stays usable,
+ * and the call's outputs are invalid.  For each kernel whose bit is set in
+ * `kernels`, one thread per CTA withholds one arrival on a barrier nothing
+ * else completes, so that a wait can only run out:
+ *   DSV4B_STALL_DECODE      decode: the first Q^T arrival (status:
+ *                           dsv4b_read_kernel_status);
+ *   DSV4B_STALL_KV_WRITE    KV-cache writer: the first chunk's copies
+ *                           (status: dsv4b_kv_cache_write_status);
+ *   DSV4B_STALL_MQA_LOGITS  indexer logits: the first page-id batch
+ *                           (status: dsv4b_mqa_logits_status).
+ * A test sets a bit, runs the call (about 2-4 s), checks the status, then
+ * clears the hook (kernels = 0).  Replaces nothing in the reference, whose
+ * kernels have no bounded waits (csrc/common/defines.h:11-21 aborts the
+ * process on CUDA errors instead). */
+#define DSV4B_STALL_DECODE 1
+#define DSV4B_STALL_KV_WRITE 2
+#define DSV4B_STALL_MQA_LOGITS 4
+DSV4B_API int dsv4b_set_test_stall(int kernels);
+
 /* Size of the library's built-in device scratch used by
- * dsv4b_sparse_decode_noalloc (32 MiB per GPU that loads the library). */
+ * dsv4b_sparse_decode_noalloc (32 MiB on each GPU where the library's
+ * device code has been loaded). */
 #define DSV4B_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* Sparse decode forward that allocates nothing.  No counterpart in the
@@ -289,9 +317,15 @@ DSV4B_API int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes,
  * status word live in a fixed DSV4B_NOALLOC_SCRATCH_BYTES array inside the
  * library instead of a caller workspace; requests whose workspace
  * (dsv4b_workspace_bytes) would exceed it return DSV4B_ERR_SCRATCH_LIMIT
- * before launching anything.  The first call on a device looks up that
- * device's scratch address (a one-time runtime query, no allocation), so
- * make the first call on each device before any stream capture.  All calls
+ * before launching anything.  The scratch is device memory of the library's
+ * module: CUDA allocates it when it loads the module on a device, which
+ * with lazy module loading (the CUDA default) happens at the first call of
+ * the library that touches that device, not when the library is opened.  So
+ * make one call of this function on each device BEFORE sizing a KV-cache
+ * pool from the free memory, and before any stream capture; from then on a
+ * call allocates nothing (cudaMemGetInfo does not change across calls).
+ * Read a call's status word with dsv4b_read_kernel_status(NULL, 0, ...).
+ * All calls
  * on a device share the one scratch array and it keeps the last call's
  * contents (the status word is cleared at the start of every call): calls
  * that overlap on the GPU -- different streams without ordering between

@@ -49,3 +49,30 @@ def assert_matches(out, lse, ref_out, ref_lse):
     l = lse.float().cpu().numpy().transpose(0, 2, 1)
     np.testing.assert_allclose(o, ref_out, atol=OUT_ATOL, rtol=OUT_RTOL)
     np.testing.assert_allclose(l, ref_lse, atol=LSE_ATOL, rtol=LSE_RTOL)
+
+
+def oracle_rows_v32(bt, rows):
+    """Oracle output for selected query rows of a full-size V32 batch
+    without copying the whole cache to the host: the rows' referenced cache
+    records are gathered on the device into a compact cache (one token per
+    page) and the indices remapped to it.  `rows` are (b, s) pairs.
+    Returns (out [n, h_q, 512], lse [n, h_q]) as numpy."""
+    kv_flat = bt.kv.view(-1, 656)
+    n_tok = kv_flat.shape[0]
+    idx = torch.stack([bt.indices[b_, s_] for b_, s_ in rows]).long()      # [n, topk]
+    valid = (idx >= 0) & (idx < n_tok)
+    uniq, inv = torch.unique(torch.where(valid, idx, torch.zeros_like(idx)), return_inverse=True)
+    compact = kv_flat[uniq].contiguous().view(-1, 1, 1, 656)
+    remap = torch.where(valid, inv, torch.full_like(inv, -1)).to(torch.int32)
+    q = torch.stack([bt.q[b_, s_] for b_, s_ in rows]).unsqueeze(1)         # [n, 1, h_q, 576]
+    out, lse = oracle_for(q, compact, remap.unsqueeze(1), None, bt.attn_sink, bt.sm_scale, "v32")
+    return out[:, 0], lse[:, 0]
+
+
+def assert_rows_match(out, lse, bt, rows):
+    """Checks selected (b, s) rows of a decode result against oracle_rows_v32."""
+    ref_out, ref_lse = oracle_rows_v32(bt, rows)
+    o = np.stack([out[b_, s_].float().cpu().numpy() for b_, s_ in rows])
+    l = np.stack([lse[b_, :, s_].float().cpu().numpy() for b_, s_ in rows])
+    np.testing.assert_allclose(o, ref_out, atol=OUT_ATOL, rtol=OUT_RTOL)
+    np.testing.assert_allclose(l, ref_lse, atol=LSE_ATOL, rtol=LSE_RTOL)

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from dsv4b_testutil import LSE_ATOL, LSE_RTOL, OUT_ATOL, OUT_RTOL, assert_matches, oracle_for
+from dsv4b_testutil import LSE_ATOL, LSE_RTOL, OUT_ATOL, OUT_RTOL, assert_matches, assert_rows_match, oracle_for
 from golden_io import golden_names, load_golden
 from oracle import schedule_oracle as SO
 from oracle import sparse_decode_oracle as O
@@ -225,10 +225,9 @@ def test_config1_full_size_properties():
     kc = _kc()
     bt = kc.make_batch(kc.CONFIGS[1])
     out, lse, tsm, ns = _run(bt)
-    rows = [0, 17, 31]
-    ref_out, ref_lse = oracle_for(bt.q[rows], bt.kv, bt.indices[rows], None, bt.attn_sink,
-                                  bt.sm_scale, "v32")
-    assert_matches(out[rows], lse[rows], ref_out, ref_lse)
+    # eight rows; in the cluster plan every row is split over the 4 ranks of
+    # its cluster, so each row checks the cross-rank merge of all 512 dims
+    assert_rows_match(out, lse, bt, [(r, 0) for r in (0, 5, 9, 13, 17, 22, 26, 31)])
     # permuting the top-k order changes nothing but summation order
     perm = torch.randperm(bt.indices.shape[-1], device="cuda")
     out2, lse2, _, _ = _run(kc.Batch(bt.q, bt.kv, bt.indices[..., perm].contiguous(), bt.attn_sink,
@@ -242,6 +241,32 @@ def test_config1_full_size_properties():
     _, lse_ns, _, _ = _run(kc.Batch(bt.q, bt.kv, bt.indices, None, bt.sm_scale, bt.spec))
     want = torch.logaddexp(lse_ns, torch.full_like(lse_ns, math.log(128.0)))
     torch.testing.assert_close(lse3, want, atol=2e-4, rtol=1e-4)
+
+
+def test_config2_full_size_matches_oracle():
+    """BASELINE config 2 exactly (b 8, s_q 2, h_q 128, top-k 2048, 50 %
+    overlap between the two draft rows, 393,216-token cache per request):
+    every query row against the oracle, both head groups."""
+    kc = _kc()
+    bt = kc.make_batch(kc.CONFIGS[2])
+    out, lse, _, _ = _run(bt)
+    assert_rows_match(out, lse, bt, [(b_, s_) for b_ in range(8) for s_ in range(2)])
+
+
+def test_config4_full_size_sampled_rows():
+    """BASELINE config 4 on one GPU (b 256, h_q 128, top-k 2048, 64K
+    contexts, an 11 GB cache): the contiguous split plan with the combine
+    kernel.  Sixteen rows, including the rows that hold part boundaries of
+    the schedule (split rows merged by the combine), against the oracle."""
+    from deepseek_v4_kernel import ops
+    kc = _kc()
+    bt = kc.make_batch(kc.CONFIGS[4])
+    out, lse, tsm, ns = _run(bt)
+    splits = ns.cpu().numpy()
+    split_rows = [r for r in range(256) if splits[r + 1] - splits[r] > 1]
+    assert split_rows, "config 4 is expected to split rows across parts"
+    pick = sorted(set(split_rows[:6] + split_rows[-4:] + [0, 1, 100, 128, 200, 255]))[:16]
+    assert_rows_match(out, lse, bt, [(r, 0) for r in pick])
 
 
 # ---------------------------------------------------------------- graphs + interface

@@ -9,8 +9,11 @@ this entry point uses it in place of a caller workspace.  The test calls it
 through the C ABI twice in a row (on two different batches, so stale
 scratch contents from the first call cannot leak into the second) and
 checks each result against the workspace entry point dsv4b_sparse_decode
-on the same inputs, within the tolerances the other GPU tests use.  It
-also checks that an oversized request is refused before any launch.
+on the same inputs, within the tolerances the other GPU tests use, that
+the free device memory does not change across a repeated call, and that the
+noalloc status word (read with dsv4b_read_kernel_status(NULL, 0, ...)) is
+clear after each call.  It also checks that an oversized request is
+refused before any launch.
 
 The file name makes pytest collect it last, so a run stopped by a failure
 here has already run every other test; it also passes alone in a fresh
@@ -47,8 +50,21 @@ def _both_paths(bt):
             rc = lib.dsv4b_sparse_decode(ctypes.byref(p), tsm.data_ptr(), ns.data_ptr(), parts,
                                          ws.data_ptr(), ws.numel(), stream)
         else:
-            rc = lib.dsv4b_sparse_decode_noalloc(ctypes.byref(p), tsm.data_ptr(), ns.data_ptr(),
-                                                 parts, stream)
+            # Twice: the first call of a process may still load code lazily
+            # (the documented reason to make it before sizing a KV pool);
+            # the second must leave the free device memory unchanged.
+            for call in range(2):
+                torch.cuda.synchronize()
+                free0 = torch.cuda.mem_get_info(dev)[0]
+                rc = lib.dsv4b_sparse_decode_noalloc(ctypes.byref(p), tsm.data_ptr(), ns.data_ptr(),
+                                                     parts, stream)
+                torch.cuda.synchronize()
+                free1 = torch.cuda.mem_get_info(dev)[0]
+                if call == 1:
+                    assert free1 == free0, f"a repeated noalloc call changed free memory by {free0 - free1} B"
+                flags = ctypes.c_int(-1)
+                assert lib.dsv4b_read_kernel_status(None, 0, ctypes.byref(flags), stream) == 0
+                assert flags.value == 0, "a wait of the noalloc call timed out"
         assert rc == 0, _lib.STATUS.get(rc, rc)
         torch.cuda.synchronize()
         outs[name] = (out, lse)
