@@ -3,7 +3,7 @@
 "sparse-decode us/step & % roofline").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1|2|4] [--mode batch|head]
+                    [--config 1|2|4] [--mode batch|head|replicate]
 
 A step is one pass of the hot path over one batch: the decode kernel (K1)
 plus the split combine (K3), on the schedule that get_mla_metadata (K2)
@@ -15,16 +15,28 @@ cache), synthetic seeded data.  L2 is flushed (256 MiB write) before every
 timed step; the gathered KV (43 MB) is below L2 size, so without the flush
 the rows would be L2-resident across steps.
 
-N > 1 (torchrun, one rank per GPU): "batch" mode shards requests -- every
-rank runs its own config-sized batch on its own cache (weak scaling, no
-collective in the data path); "head" mode splits h_q over the ranks with a
-replicated cache and all-gathers the bf16 outputs with NCCL (verification
-traffic, outside the timed step).  Timing: CUDA events on the launching
-stream, max over ranks.
+N > 1 (torchrun, one rank per GPU).  "batch" mode (default) shards the
+requests of one global batch: rank r builds only requests
+partition.batch_range(B, r, N) and their cache pages (each request is
+generated from its own seed, so the shards are exactly the unsharded
+batch's requests) and decodes them; no collective in the data path.
+Configs 1-3 are one GPU's batch, so B = b x N (weak scaling); config 4 is
+the whole-box batch, B = 256 over all ranks (strong scaling).  "head" mode
+splits h_q over the ranks with a replicated cache.  After the timed region
+(batch and head) the shards are all-gathered with NCCL and rank 0 compares
+sampled rows with an unsharded decode of the same requests
+("partition_check").  "replicate" runs an independent config-sized batch
+per rank.  Timing: CUDA events on the launching stream, max over ranks.
+
+The default run (config 1, no overrides) also carries, at N = 1, configs 2
+and 4 ("other_configs") and the writer / indexer next to the decode
+("next_rows"); at N > 1, config 4 batch- and head-sharded
+("partition_config4").
 
 --impl reference times the CPU oracle port (oracle/, a numpy restatement
 of the reference's tests/reference.py) on this host's cores on the same
-workload; rank 0 only.
+workload (the global batch of the mode); rank 0 only.  It imports only
+host-side modules of the package, so libdsv4b.so is not loaded.
 """
 from __future__ import annotations
 
@@ -56,7 +68,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
                     help="BASELINE config; 3 = the CUDA-graph batch x context sweep")
-    ap.add_argument("--mode", choices=["batch", "head"], default="batch")
+    ap.add_argument("--mode", choices=["batch", "head", "replicate"], default="batch",
+                    help="N > 1: batch = shard the requests of one global batch; head = shard h_q over "
+                         "a replicated cache; replicate = an independent batch per rank")
     ap.add_argument("--batch", type=int, default=None, help="override b (per rank)")
     ap.add_argument("--ctx", type=int, default=None,
                     help="override the per-request context (cache size); same per-step work "
@@ -170,15 +184,54 @@ def bind_to_gpu_numa_node(device_index: int):
 
 
 # ------------------------------------------------------------------ workload
-def workload(cfg: int, batch_override, rank: int, ctx_override=None):
+# Config 4 is the whole-box batch (b = 256 requests over all ranks, strong
+# scaling); the other configurations are one GPU's batch, so in batch mode
+# the global batch is b x N requests (weak scaling: per-GPU work fixed).
+WHOLE_BOX_CONFIGS = (4,)
+
+
+def workload(cfg: int, batch_override, ctx_override=None):
+    """The configuration's BatchSpec (b = the per-GPU batch, or for config
+    4 the whole-box batch)."""
     from deepseek_v4_kernel import kvcache
     spec = kvcache.sweep_spec(32, 131072) if cfg == 3 else kvcache.CONFIGS[cfg]
-    spec = kvcache.BatchSpec(**{**spec.__dict__, "seed": 1000 + rank})
+    spec = kvcache.BatchSpec(**{**spec.__dict__, "seed": 1000})
     if batch_override:
         spec.b = batch_override
     if ctx_override:
         spec.ctx, spec.cache_ctx = ctx_override, None
     return spec
+
+
+def global_batch(cfg: int, spec, mode: str, world: int):
+    """(global BatchSpec, requests per step over all ranks) for a mode."""
+    from deepseek_v4_kernel import kvcache
+    if mode == "batch" and cfg not in WHOLE_BOX_CONFIGS:
+        return kvcache.BatchSpec(**{**spec.__dict__, "b": spec.b * world}), spec.b * world
+    if mode == "replicate":
+        return spec, spec.b * world
+    return spec, spec.b
+
+
+def scaling_kind(cfg: int, mode: str) -> str:
+    if mode == "head" or (mode == "batch" and cfg in WHOLE_BOX_CONFIGS):
+        return "strong"
+    return "weak"
+
+
+def build_inputs(spec_g, mode: str, rank: int, world: int, device):
+    """This rank's batch.  batch: requests batch_range(b, rank, N) of the
+    global batch, built by this rank alone; head: the whole batch on every
+    rank (replicated cache; the rank decodes its head slice); replicate:
+    an independent config-sized batch per rank (seed 1000 + rank)."""
+    from deepseek_v4_kernel import kvcache, partition
+    if mode == "batch":
+        lo, hi = partition.batch_range(spec_g.b, rank, world)
+        return kvcache.make_batch_shard(spec_g, lo, hi, device=device), (lo, hi)
+    if mode == "head":
+        return kvcache.make_batch_shard(spec_g, 0, spec_g.b, device=device), (0, spec_g.b)
+    s = kvcache.BatchSpec(**{**spec_g.__dict__, "seed": 1000 + rank})
+    return kvcache.make_batch(s, device=device), (0, s.b)
 
 
 def algorithmic(spec, h_q_local=None):
@@ -191,61 +244,69 @@ def algorithmic(spec, h_q_local=None):
     return kv_bytes, flops
 
 
-def workload_name(spec, mode, world):
-    return (f"b{spec.b} s_q{spec.s_q} h_q{spec.h_q} "
+def workload_name(spec, mode, world, b_global=None):
+    return (f"b{b_global or spec.b} s_q{spec.s_q} h_q{spec.h_q} "
             f"topk{spec.topk} ctx{spec.ctx} page{spec.page_block} {spec.layout.upper()} fp8 KV"
             + (f", {mode}-sharded x{world}" if world > 1 else ""))
 
 
 # ------------------------------------------------------------------ reference arm (CPU oracle)
 def run_reference(args, spec, world, rank):
+    """The reference's CPU path (the numpy port of tests/reference.py) on
+    this host's cores, for the same workload as our arm: the global batch of
+    the run's mode, a bounded sample of whole query rows per step, times
+    scaled to the full global batch."""
     if rank != 0:
         return
-    import numpy as np
     import torch
     from threadpoolctl import threadpool_limits
     from concurrent.futures import ThreadPoolExecutor
 
-    from deepseek_v4_kernel import kvcache
+    from deepseek_v4_kernel import kvcache  # host-only module: does not map libdsv4b.so
     from oracle import sparse_decode_oracle as O
 
+    spec_g, reqs = global_batch(args.config, spec, args.mode, world)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    bt = kvcache.make_batch(spec, device=dev)
-    q = bt.q.float().cpu().numpy()
-    kv = bt.kv.cpu().numpy()
-    idx = bt.indices.cpu().numpy()
-    sink = bt.attn_sink.cpu().numpy() if bt.attn_sink is not None else None
-    del bt
     threads = os.cpu_count() or 1
 
-    def one(rows):
-        return O.sparse_decode_reference(q[rows], kv, idx[rows], None, sink, 1.0 / math.sqrt(q.shape[-1]),
-                                         spec.page_block, layout=spec.layout)
+    def load(lo, hi):
+        bt = kvcache.make_batch_shard(spec_g, lo, hi, device=dev)
+        return (bt.q.float().cpu().numpy(), bt.kv.cpu().numpy(), bt.indices.cpu().numpy(),
+                bt.attn_sink.cpu().numpy() if bt.attn_sink is not None else None, bt.sm_scale)
 
-    # bounded sample: as many whole query rows as fit in ~2 s per step
+    def one(data, rows):
+        q, kv, idx, sink, scale = data
+        return O.sparse_decode_reference(q[rows], kv, idx[rows], None, sink, scale, spec.page_block,
+                                         layout=spec.layout)
+
+    # bounded sample: as many whole requests as fit in ~2 s per step
+    first = load(0, 1)
     t0 = time.perf_counter()
     with threadpool_limits(1):
-        one([0])
+        one(first, [0])
     per_row = max(time.perf_counter() - t0, 1e-4)
-    n_rows = int(min(spec.b, max(1, threads * 2.0 / per_row)))
+    n_rows = int(min(reqs, spec_g.b, max(1, threads * 2.0 / per_row)))
+    data = load(0, n_rows) if n_rows > 1 else first
     chunks = [list(range(i, n_rows, threads)) for i in range(min(threads, n_rows))]
     times = []
     with threadpool_limits(1), ThreadPoolExecutor(threads) as ex:
         for i in range(args.warmup + args.steps):
             t = time.perf_counter()
-            list(ex.map(one, chunks))
+            list(ex.map(lambda c: one(data, c), chunks))
             dt = time.perf_counter() - t
             if i >= args.warmup:
-                times.append(dt * spec.b / n_rows)       # scaled to the full batch
+                times.append(dt * reqs / n_rows)       # scaled to the full global batch
     us = statistics.median(times) * 1e6
-    sample = (f"{n_rows} of {spec.b} query rows per step (times scaled to the full batch), "
-              f"numpy oracle port of tests/reference.py, gather of the top-k rows only")
+    sample = (f"{n_rows} of {reqs} requests per step (times scaled to the full batch of the run), "
+              f"numpy port of tests/reference.py, gather of the top-k rows only")
     line = {
         "metric": "sparse_decode_us_per_step", "value": round(us, 1), "unit": "us/step",
         "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
+        "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
+        "scaling": scaling_kind(args.config, args.mode),
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, 1), "cpu_threads": threads},
+        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, world, reqs),
+                   "cpu_threads": threads},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
@@ -292,22 +353,60 @@ def cpu_baseline_quick(spec, bt, budget_s=12.0):
 
 
 # ------------------------------------------------------------------ our arm
+def verify_partition(args, spec_g, out, lse, h_range, world, rank, device):
+    """Outside the timed region: reassemble the shards with NCCL and compare
+    sampled rows with an unsharded decode of the same requests (our public
+    op on one GPU).  Returns a summary on rank 0, None elsewhere."""
+    import torch
+    from deepseek_v4_kernel import kvcache, ops, partition
+    if args.mode == "batch":
+        out_all = partition.all_gather_batch(out, spec_g.b, world)
+        lse_all = partition.all_gather_batch(lse, spec_g.b, world)
+        if rank != 0:
+            return None
+        b = spec_g.b
+        picks = sorted({0, b // 3, (2 * b) // 3, b - 1})
+        errs = []
+        for r in picks:
+            one = kvcache.make_batch_shard(spec_g, r, r + 1, device=device)
+            o, l, _, _ = ops.sparse_decode_fwd(one.q, one.kv, one.indices, None, one.attn_sink, None, None,
+                                               None, None, None, 512, one.sm_scale)
+            errs.append(((out_all[r].float() - o[0].float()).abs().max().item(),
+                         (lse_all[r] - l[0]).abs().max().item()))
+        what = f"requests {picks} of the all-gathered batch vs each request decoded alone"
+    else:  # head
+        full = partition.all_gather_heads(out, world)
+        if rank != 0:
+            return None
+        bt, _ = build_inputs(spec_g, "head", 0, 1, device)
+        o, l, _, _ = ops.sparse_decode_fwd(bt.q, bt.kv, bt.indices, None, bt.attn_sink, None, None,
+                                           None, None, None, 512, bt.sm_scale)
+        errs = [((full.float() - o.float()).abs().max().item(), 0.0)]
+        what = "all-gathered head shards vs the unsharded decode (all heads, one GPU)"
+    max_out = max(e[0] for e in errs)
+    max_lse = max(e[1] for e in errs)
+    return {"checked": what, "max_abs_err_out": max_out, "max_abs_err_lse": max_lse,
+            "ok": bool(max_out <= 2e-2 and max_lse <= 1e-3)}
+
+
 def run_ours(args, spec, world, rank, local_rank):
+    """Times the decode step of this rank's shard; returns the JSON line on
+    rank 0 (None on the other ranks)."""
     import torch
     import torch.distributed as dist
 
     import deepseek_v4_kernel as dk
-    from deepseek_v4_kernel import _lib, kvcache, ops
+    from deepseek_v4_kernel import _lib, ops, partition
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     lib = _lib.lib
     assert lib.dsv4b_check_device(local_rank) == 0, "not an sm_100 GPU"
 
-    bt = kvcache.make_batch(spec, device=device)
+    spec_g, reqs = global_batch(args.config, spec, args.mode, world)
+    bt, (r_lo, r_hi) = build_inputs(spec_g, args.mode, rank, world, device)
     h_lo, h_hi = 0, spec.h_q
     if args.mode == "head" and world > 1:
-        from deepseek_v4_kernel import partition
         h_lo, h_hi = partition.head_range(spec.h_q, rank, world)
     q = bt.q[:, :, h_lo:h_hi].contiguous()
     sink = bt.attn_sink[h_lo:h_hi].contiguous() if bt.attn_sink is not None else None
@@ -378,22 +477,18 @@ def run_ours(args, spec, world, rank, local_rank):
         dist.barrier()
     clocks = sampler.stop()
     dec_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    step_ms = dec_ms  # evs[1] follows the step's last launch directly
-    t_step = statistics.median(step_ms)
-    t_dec = statistics.median(dec_ms)
+    t_step = statistics.median(dec_ms)  # evs[1] follows the step's last launch directly
     assert dk.read_kernel_status(device) == 0, "kernel wait timeout"
 
-    # head mode: all-gather the head shards (verification traffic, untimed)
-    if args.mode == "head" and world > 1:
-        from deepseek_v4_kernel import partition
-        full = partition.all_gather_heads(out, world)
-        assert full.shape[2] == spec.h_q
+    verify = None
+    if world > 1 and args.mode in ("batch", "head"):
+        verify = verify_partition(args, spec_g, out, lse, (h_lo, h_hi), world, rank, device)
 
     # max over ranks
     if world > 1:
-        t = torch.tensor([t_step, t_dec], dtype=torch.float64, device=device)
+        t = torch.tensor([t_step], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_dec = t.tolist()
+        t_step = t.item()
 
     # e2e through the public API with host buffers
     e2e = None
@@ -428,28 +523,39 @@ def run_ours(args, spec, world, rank, local_rank):
             ev[i][1].record(stream)
         torch.cuda.synchronize()
         t_e2e = statistics.median([a.elapsed_time(b_) for a, b_ in ev])
+        # host wall clock: n back-to-back steps, no flush between them, one
+        # synchronise at the end (exposes the host-side enqueue cost)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            e2e_step()
+        torch.cuda.synchronize()
+        t_wall = (time.perf_counter() - t0) / n_e2e * 1e3
         if world > 1:
-            t = torch.tensor([t_e2e], dtype=torch.float64, device=device)
+            t = torch.tensor([t_e2e, t_wall], dtype=torch.float64, device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t_e2e = t.item()
+            t_e2e, t_wall = t.tolist()
         h2d = q_host.numel() * q_host.element_size() + idx_host.numel() * idx_host.element_size()
         d2h = out_host.numel() * out_host.element_size() + lse_host.numel() * lse_host.element_size()
         e2e = {"value": round(t_e2e * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h,
+               "wall_us": round(t_wall * 1e3, 2),
                "path": "deepseek_v4_kernel.flash_mla_with_kvcache (FlashMLASchedMeta reused), "
                        "pinned host q/indices -> device, out/lse -> pinned host",
+               "timing": "value: CUDA events around each step (L2 flushed before it); wall_us: host "
+                         f"perf_counter over {n_e2e} back-to-back steps with no flush, one sync at the end",
                "host_numa_node": numa_node}
 
     if rank != 0:
-        return
+        return None
     hbm_peak, tc_peak, peak_src = measured_peaks()
-    kv_bytes, flops = algorithmic(spec, h_q)
-    achieved_gbs = kv_bytes / (t_dec * 1e-3) / 1e9
-    achieved_tf = flops / (t_dec * 1e-3) / 1e12
+    kv_bytes, flops = algorithmic(bt.spec, h_q)
+    achieved_gbs = kv_bytes / (t_step * 1e-3) / 1e9
+    achieved_tf = flops / (t_step * 1e-3) / 1e12
     bound = "hbm" if kv_bytes / hbm_peak / 1e9 >= flops / tc_peak / 1e12 else "tensor"
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
+    if os.path.exists(tpath) and world == 1:
         try:
             traffic = json.load(open(tpath)).get(f"config{args.config}")
         except Exception:
@@ -461,13 +567,14 @@ def run_ours(args, spec, world, rank, local_rank):
         roof = {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
                 "frac": round(achieved_tf / tc_peak, 4), "traffic": traffic}
     roof["peak_source"] = peak_src
-    roof["kernel"] = "sparse_decode_kernel (K1)"
+    roof["kernel"] = "sparse_decode_kernel (K1)" + (" + combine_kernel (K3)" if launches_per_step > 1 else "")
+    roof["per"] = "rank 0's shard" if world > 1 else "the whole batch"
     roof["algorithmic_bytes_per_launch"] = kv_bytes
     roof["algorithmic_flops_per_launch"] = flops
     roof["tensor_frac"] = round(achieved_tf / tc_peak, 4)
     roof["hbm_frac"] = round(achieved_gbs / hbm_peak, 4)
     t_roof_us = max(kv_bytes / hbm_peak / 1e3, flops / tc_peak / 1e6)
-    tokens = spec.b * spec.s_q * world if args.mode == "batch" else spec.b * spec.s_q
+    tokens = reqs * spec.s_q
     line = {
         "metric": "sparse_decode_us_per_step",
         "value": round(t_step * 1e3, 2),
@@ -477,15 +584,16 @@ def run_ours(args, spec, world, rank, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(t_step, 5),
         "higher_is_better": False,
-        "scaling": "weak" if args.mode == "batch" else "strong",
+        "scaling": scaling_kind(args.config, args.mode),
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q / latent / RoPE, random page tables, distinct top-k)",
-        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, world),
+        "config": {"workload": f"config{args.config}: " + workload_name(spec, args.mode, world, reqs),
                    "l2": "flushed before every step (256 MiB write)",
                    "parallelism": f"{args.mode}-shard x{world}" if world > 1 else "single GPU",
+                   "rank0_requests": [r_lo, r_hi], "rank0_heads": [h_lo, h_hi],
                    "num_sm_parts": parts, "cluster_size": cluster},
-        "decode_kernel_us": round(t_dec * 1e3, 2),
+        "decode_kernel_us": round(t_step * 1e3, 2),
         "combine_launched": launches_per_step > 1,
         "sched_meta_us": round(sched_us, 2),
         "roofline_time_us": round(t_roof_us, 2),
@@ -495,20 +603,53 @@ def run_ours(args, spec, world, rank, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if verify is not None:
+        line["partition_check"] = verify
     if e2e:
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_quick(spec, bt)
-    if world == 1 and args.config == 1 and not args.no_next_rows:
-        line["next_rows"] = next_rows(args)
-    print(json.dumps(line), flush=True)
-    if args.json_out:
-        with open(args.json_out, "w") as f:
-            f.write(json.dumps(line) + "\n")
+        line["cpu_baseline"] = cpu_baseline_quick(bt.spec, bt)
+    return line
+
+
+def summary_of(line):
+    """The fields of a sub-run's line carried under another line's key."""
+    keep = ("value", "unit", "n_gpus", "scaling", "decode_kernel_us", "combine_launched", "tokens_per_s",
+            "roofline_time_us", "step_roofline_frac", "gpu_launches", "clocks", "partition_check")
+    d = {k: line[k] for k in keep if k in line}
+    d["workload"] = line["config"]["workload"]
+    d["parallelism"] = line["config"]["parallelism"]
+    r = line["roofline"]
+    d["roofline"] = {k: r[k] for k in ("bound", "achieved", "peak", "unit", "frac", "hbm_frac", "tensor_frac")}
+    return d
+
+
+def sub_runs(args, world, rank, local_rank):
+    """Extra workloads carried by the default line: at N = 1 configs 2 and
+    4 on one GPU; at N > 1 config 4's whole-box batch, batch-sharded and
+    head-sharded.  20 timed steps each, no e2e / CPU baseline."""
+    import copy
+    import torch
+    plan = ([(2, "batch"), (4, "batch")] if world == 1 else [(4, "batch"), (4, "head")])
+    out = {}
+    for cfg, mode in plan:
+        a = copy.copy(args)
+        a.config, a.mode, a.steps, a.warmup = cfg, mode, 20, 5
+        a.no_e2e, a.no_cpu_baseline, a.batch, a.ctx = True, True, None, None
+        key = f"config{cfg}" + ("" if world == 1 else f"_{mode}")
+        try:
+            line = run_ours(a, workload(cfg, None), world, rank, local_rank)
+            if line is not None:
+                out[key] = summary_of(line)
+        except Exception as e:  # reported in the line, the headline stands
+            out[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
+    return out
 
 
 def next_rows(args):
-    """The two steps either side of the decode (SURVEY next rows), measured
+    """The two steps either side of the decode in a serving step (the cache
+    write before it, the indexer that picks its top-k), measured
     with their own bench modes and summarised in the headline line: the
     KV-cache writer (131,072 tokens, V32 and MODEL1) and the indexer logits
     (config 1's contexts).  A failure here is reported, not raised."""
@@ -853,7 +994,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    spec = workload(args.config, args.batch, rank if args.mode == "batch" else 0, args.ctx)
+    spec = workload(args.config, args.batch, args.ctx)
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, spec, world, rank)
@@ -864,7 +1005,21 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, spec, world, rank, local_rank)
+        line = run_ours(args, spec, world, rank, local_rank)
+        default_run = args.config == 1 and args.batch is None and args.ctx is None and not args.no_next_rows
+        if default_run:
+            import torch
+            torch.cuda.empty_cache()
+            extra = sub_runs(args, world, rank, local_rank)
+            if line is not None:
+                line["other_configs" if world == 1 else "partition_config4"] = extra
+                if world == 1:
+                    line["next_rows"] = next_rows(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+            if args.json_out:
+                with open(args.json_out, "w") as f:
+                    f.write(json.dumps(line) + "\n")
     finally:
         if world > 1:
             import torch.distributed as dist

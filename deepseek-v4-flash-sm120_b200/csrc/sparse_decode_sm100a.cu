@@ -178,14 +178,6 @@ __device__ __forceinline__ int empty_of(int c) {
 // columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
 // pair one PV M-block releases.
 //
-// Gather mapping.  Producer warp w owns tile rows 16w..16w+15 and handles
-// four of them per pass: in pass k lane l works on row 16w + 4k + (l >> 3)
-// and on the 16-byte column q = l & 7 of a 128-byte block of that row.  A
-// warp load instruction therefore reads four rows x 128 contiguous bytes
-// (whole 32-byte sectors), and the unit of work is a "chunk pair": 128
-// columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
-// pair one PV M-block releases.
-//
 // Loads are split in two register phases per tile.  Phase A (pairs 0-1 and
 // the scales) is issued at the end of the previous tile together with an
 // L2 bulk prefetch of each whole row, and landed there.  Phase B (pairs 2-3

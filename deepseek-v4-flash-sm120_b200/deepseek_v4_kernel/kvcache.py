@@ -153,6 +153,77 @@ def make_batch(spec: BatchSpec, device="cuda", chunk_tokens: int = 1 << 20) -> B
                  sm_scale=1.0 / math.sqrt(d_qk), spec=spec)
 
 
+def _request_indices(spec: BatchSpec, g: torch.Generator, device) -> torch.Tensor:
+    """Logical top-k positions [s_q, topk] of one request: distinct uniform
+    positions in [0, ctx) per draft row, row s > 0 sharing
+    round(draft_overlap * topk) of row 0's positions."""
+    idx = torch.empty(spec.s_q, spec.topk, dtype=torch.int64, device=device)
+    base = torch.randperm(spec.ctx, generator=g, device=device)[: spec.topk]
+    idx[0] = base
+    n_share = int(round(spec.draft_overlap * spec.topk))
+    for si in range(1, spec.s_q):
+        if n_share:
+            mask = torch.ones(spec.ctx, dtype=torch.bool, device=device)
+            mask[base] = False
+            pool = torch.nonzero(mask).squeeze(1)
+            pick = pool[torch.randperm(pool.numel(), generator=g, device=device)[: spec.topk - n_share]]
+            row = torch.cat([base[:n_share], pick])
+            idx[si] = row[torch.randperm(spec.topk, generator=g, device=device)]
+        else:
+            idx[si] = torch.randperm(spec.ctx, generator=g, device=device)[: spec.topk]
+    return idx
+
+
+def make_batch_shard(spec: BatchSpec, lo: int, hi: int, device="cuda") -> Batch:
+    """Requests [lo, hi) of the global batch `spec` (spec.b requests), built
+    so that any rank can build its own shard alone: request r's q, cache
+    rows and top-k positions come from a generator seeded by (spec.seed, r)
+    only, so the rows of a request are the same bytes in every shard that
+    holds it (and in the unsharded batch, lo = 0, hi = spec.b).  The shard's
+    cache holds only its requests' pages, placed by a random permutation of
+    the shard's pages (the block tables are random page permutations, as in
+    make_batch).  attn_sink is seeded by spec.seed alone (one per model)."""
+    if not 0 <= lo < hi <= spec.b:
+        raise ValueError(f"bad request range [{lo}, {hi}) of {spec.b}")
+    nreq = hi - lo
+    d_qk = 576 if spec.layout == "v32" else 512
+    bpt = 656 if spec.layout == "v32" else 584
+    cache_ctx = spec.cache_ctx or spec.ctx
+    P = spec.page_block
+    ppr = -(-cache_ctx // P)
+    num_blocks = nreq * ppr
+    g_place = torch.Generator(device=device).manual_seed(spec.seed * 7919 + lo * 104729 + hi)
+    perm = torch.randperm(num_blocks, generator=g_place, device=device).view(nreq, ppr)
+    q = torch.empty(nreq, spec.s_q, spec.h_q, d_qk, dtype=torch.bfloat16, device=device)
+    idx = torch.empty(nreq, spec.s_q, spec.topk, dtype=torch.int64, device=device)
+    if spec.layout == "v32":
+        kv = torch.empty(num_blocks, P, 656, dtype=torch.uint8, device=device)
+    else:
+        kv = torch.empty(num_blocks, P * 584, dtype=torch.uint8, device=device)
+    for i, r in enumerate(range(lo, hi)):
+        g = torch.Generator(device=device).manual_seed(spec.seed * 1000003 + r)
+        q[i] = torch.randn(spec.s_q, spec.h_q, d_qk, generator=g, device=device).to(torch.bfloat16)
+        n = ppr * P
+        if spec.layout == "v32":
+            rows = quantize_v32(torch.randn(n, 512, generator=g, device=device),
+                                torch.randn(n, 64, generator=g, device=device).to(torch.bfloat16))
+            kv[perm[i]] = rows.view(ppr, P, 656)
+        else:
+            kv[perm[i]] = quantize_model1_pages(torch.randn(n, 448, generator=g, device=device),
+                                                torch.randn(n, 64, generator=g, device=device).to(torch.bfloat16),
+                                                P)
+        idx[i] = _request_indices(spec, g, device)
+    page = perm.gather(1, (idx // P).view(nreq, -1)).view_as(idx)
+    flat = (page * P + idx % P).to(torch.int32)
+    if spec.invalid_tail:
+        flat[..., -spec.invalid_tail:] = -1
+    g_sink = torch.Generator(device=device).manual_seed(spec.seed)
+    sink = torch.randn(spec.h_q, generator=g_sink, device=device) if spec.with_sink else None
+    shard_spec = BatchSpec(**{**spec.__dict__, "b": nreq})
+    return Batch(q=q, kv=kv.view(num_blocks, P, 1, bpt), indices=flat.contiguous(), attn_sink=sink,
+                 sm_scale=1.0 / math.sqrt(d_qk), spec=shard_spec)
+
+
 # The benchmark configurations (BASELINE.json "configs"), as BatchSpecs.
 CONFIGS = {
     0: BatchSpec(b=1, s_q=1, h_q=16, topk=128, ctx=4096, page_block=256, invalid_tail=16),
