@@ -80,7 +80,7 @@ def parse():
     ap.add_argument("--no-next-rows", action="store_true",
                     help="skip the writer / indexer summaries in the config-1 line")
     ap.add_argument("--json-out", default=None)
-    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits"], default="decode",
+    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits", "prefill"], default="decode",
                     help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
                          "logits (fp8_paged_mqa_logits) over config 1's contexts")
     ap.add_argument("--next-n", type=int, default=1, help="mqa_logits: query rows per request")
@@ -885,6 +885,86 @@ def run_mqa_logits(args):
     return line
 
 
+def run_prefill(args):
+    """One step = one flash_mla_sparse_fwd call (sparse prefill, bf16 KV):
+    s_q 4096 query tokens x h_q 128 heads, d_qk 512, top-k 2048 over a
+    65,536-row KV tensor (tensor-bound: 2.2 TFLOP per step).  --batch sets
+    s_q.  The same call of vLLM 0.22's FlashMLA kernel (a compiled library,
+    the op the serving engine runs next to the reference's decode) is timed
+    beside it when importable, as "library"."""
+    import numpy as np
+    import torch
+
+    from deepseek_v4_kernel import flash_mla_sparse_fwd
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    s_q, h_q, d, topk, s_kv = args.batch or 4096, 128, 512, 2048, 65536
+    g = torch.Generator(device=device).manual_seed(0)
+    q = torch.randn(s_q, h_q, d, generator=g, device=device).to(torch.bfloat16)
+    kv = torch.randn(s_kv, 1, d, generator=g, device=device).to(torch.bfloat16)
+    idx = torch.randint(0, s_kv, (s_q, 1, topk), generator=g, device=device, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(d)
+    out = torch.empty(s_q, h_q, 512, dtype=torch.bfloat16, device=device)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+    clk = ClockSampler(0)
+    clk.start()
+    t_ms = timed(lambda: flash_mla_sparse_fwd(q, kv, idx, scale, 512, out=out))
+    clocks = clk.stop()
+    lib = None
+    try:
+        from vllm.third_party.flashmla.flash_mla_interface import flash_mla_sparse_fwd as lib_fwd
+        lib_ms = timed(lambda: lib_fwd(q, kv, idx, scale, 512))
+        lib = {"value": round(lib_ms * 1e3, 1), "unit": "us/step",
+               "what": "vLLM 0.22 FlashMLA flash_mla_sparse_fwd (compiled library), same inputs"}
+    except Exception as e:  # not importable on this box
+        lib = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    flops = 2.0 * s_q * h_q * topk * (d + 512)
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    ach = flops / (t_ms * 1e-3) / 1e12
+    from oracle import sparse_prefill_oracle as SP
+    c0 = time.perf_counter()
+    SP.sparse_prefill_reference(q[:1].float().cpu().numpy(), kv.float().cpu().numpy(), idx[:1].cpu().numpy(), scale)
+    cpu_s = time.perf_counter() - c0
+    return {
+        "metric": "sparse_prefill_us_per_step",
+        "value": round(t_ms * 1e3, 1),
+        "unit": "us/step",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_ms, 5),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 q and KV rows, uniform random top-k rows)",
+        "config": {"workload": f"sparse prefill: s_q{s_q} h_q{h_q} d_qk{d} topk{topk} s_kv{s_kv}",
+                   "l2": "no flush (the KV tensor, 67 MB, is gathered with reuse across query tokens)"},
+        "tokens_per_s": round(s_q / (t_ms * 1e-3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(ach / tc_peak, 4), "traffic": None, "peak_source": peak_src,
+                     "kernel": "sparse_decode_kernel (bf16 prefill layout)", "algorithmic_flops_per_launch": flops},
+        "library": lib,
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": {"value": round(cpu_s * s_q * 1e6, 1), "unit": "us/step", "cores": 1, "kind": "port",
+                         "sample": f"oracle/sparse_prefill_oracle.py (float64 numpy) on 1 of the {s_q} tokens, "
+                                   f"scaled to {s_q}"},
+    }
+
+
 def run_sweep(args):
     """b in {1..32} x context in {8K..300K}, h_q 64, top-k
     2048; the whole step (flash_mla_with_kvcache with a reused
@@ -980,9 +1060,9 @@ def run_sweep(args):
 
 def main():
     args = parse()
-    if args.op in ("kv_write", "mqa_logits"):
+    if args.op in ("kv_write", "mqa_logits", "prefill"):
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            line = (run_kv_write if args.op == "kv_write" else run_mqa_logits)(args)
+            line = {"kv_write": run_kv_write, "mqa_logits": run_mqa_logits, "prefill": run_prefill}[args.op](args)
             print(json.dumps(line), flush=True)
             if args.json_out:
                 with open(args.json_out, "w") as f:

@@ -52,6 +52,7 @@ int check_cache(int layout, const void* kv, int num_blocks, int page, int64_t st
 int check_params(const dsv4b_decode_params* p) {
   if (!p) return DSV4B_ERR_INVALID_ARGUMENT;
   if (p->layout != DSV4B_LAYOUT_V32 && p->layout != DSV4B_LAYOUT_MODEL1) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->prefill || p->max_logits) return DSV4B_ERR_INVALID_ARGUMENT;  // dsv4b_sparse_prefill's fields
   if (p->b <= 0 || p->s_q <= 0 || p->h_q <= 0 || p->topk <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
   if ((int64_t)p->b * p->s_q > dsv4b::kMaxSchedRows) return DSV4B_ERR_UNSUPPORTED;
   if (p->d_v != 512) return DSV4B_ERR_UNSUPPORTED;
@@ -71,6 +72,33 @@ int check_params(const dsv4b_decode_params* p) {
                      p->stride_extra_kv_block, p->stride_extra_kv_row);
     if (rc) return rc;
   }
+  return DSV4B_OK;
+}
+
+// Sparse prefill: workspace = [status word | schedule records [rows] |
+// num_splits [rows + 1]].
+inline size_t prefill_ws_bytes(int rows) {
+  return align_up(kStatusBytes + (size_t)rows * sizeof(dsv4b_sched_meta) + ((size_t)rows + 1) * 4, 256);
+}
+
+constexpr int kMaxPrefillRows = 1 << 24;
+
+int check_prefill_params(const dsv4b_decode_params* p) {
+  if (!p) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->layout != DSV4B_LAYOUT_BF16_576 && p->layout != DSV4B_LAYOUT_BF16_512) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->prefill != 1 || p->lse_includes_sink != 0 || p->extra_kv) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->b <= 0 || p->s_q != 1 || p->h_q <= 0 || p->topk <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->b > kMaxPrefillRows || p->h_q > 65535 * 64) return DSV4B_ERR_UNSUPPORTED;
+  if (p->d_v != 512) return DSV4B_ERR_UNSUPPORTED;
+  if (p->d_qk != (p->layout == DSV4B_LAYOUT_BF16_576 ? 576 : 512)) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!p->q || !p->indices || !p->out || !p->lse || !p->kv) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->q, 16) || p->stride_q_b % 8 || p->stride_q_h % 8) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->out, 16) || p->stride_o_b % 8 || p->stride_o_h % 8) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (!aligned(p->lse, 4) || !aligned(p->indices, 4) || (p->max_logits && !aligned(p->max_logits, 4)))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  // KV rows: 16-byte aligned base and row stride (16-byte loads), a whole d_qk row each.
+  if (!aligned(p->kv, 16) || p->num_blocks <= 0 || p->page_block_size != 1) return DSV4B_ERR_INVALID_ARGUMENT;
+  if (p->stride_kv_block % 16 != 0 || p->stride_kv_block < (int64_t)p->d_qk * 2) return DSV4B_ERR_INVALID_ARGUMENT;
   return DSV4B_OK;
 }
 
@@ -375,6 +403,24 @@ int dsv4b_read_kernel_status(void* workspace, size_t workspace_bytes, int* flags
   if ((rc = cuda_rc(cudaMemcpyAsync(flags, workspace, sizeof(int), cudaMemcpyDeviceToHost, s)))) return rc;
   if ((rc = cuda_rc(cudaStreamSynchronize(s)))) return rc;
   return cuda_rc(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+}
+
+size_t dsv4b_prefill_workspace_bytes(int rows) {
+  return rows <= 0 || rows > kMaxPrefillRows ? 0 : prefill_ws_bytes(rows);
+}
+
+int dsv4b_sparse_prefill(const dsv4b_decode_params* p, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_prefill_params(p);
+  if (rc) return rc;
+  const int rows = p->b;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < prefill_ws_bytes(rows)) return DSV4B_ERR_WORKSPACE;
+  if ((rc = current_arch_ok())) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  auto* sched = reinterpret_cast<dsv4b_sched_meta*>(ws + kStatusBytes);
+  auto* num_splits = reinterpret_cast<int32_t*>(ws + kStatusBytes + (size_t)rows * sizeof(dsv4b_sched_meta));
+  if ((rc = cuda_rc(cudaMemsetAsync(ws, 0, kStatusBytes, s)))) return rc;
+  return cuda_rc(dsv4b::run_sparse_prefill(*p, sched, num_splits, reinterpret_cast<int*>(ws), s));
 }
 
 }  // extern "C"

@@ -48,10 +48,31 @@ struct LayoutT<DSV4B_LAYOUT_MODEL1> {
   static constexpr bool kPInRopeSlot = false;
 };
 
+// Sparse prefill: a bf16 [s_kv, d_qk] KV tensor; rows are copied into the
+// K tile without dequantisation.  Same chunk structure as V32 (576: the
+// RoPE chunk's slot doubles as P^T) and MODEL1 (512).
+template <>
+struct LayoutT<DSV4B_LAYOUT_BF16_576> {
+  static constexpr int kDqk = 576;
+  static constexpr int kChunks = 9;
+  static constexpr bool kPInRopeSlot = true;
+};
+template <>
+struct LayoutT<DSV4B_LAYOUT_BF16_512> {
+  static constexpr int kDqk = 512;
+  static constexpr int kChunks = 8;
+  static constexpr bool kPInRopeSlot = false;
+};
+
+__host__ __device__ constexpr bool is_bf16_layout(int L) {
+  return L == DSV4B_LAYOUT_BF16_576 || L == DSV4B_LAYOUT_BF16_512;
+}
+
 // ------------------------------------------------------------- schedule
 struct ReqInfo {
   int b, s;
   int len_main;   // attended main positions, clamped to [1, topk]
+  int len_valid;  // the same, clamped to [0, topk] (prefill masks rows past it)
   int ntm;        // main tiles
   int len_extra;  // attended extra positions, clamped to [0, extra_topk]
   int nt;         // total tiles (main then extra)
@@ -68,6 +89,7 @@ __device__ __forceinline__ ReqInfo req_info(const dsv4b_decode_params& p, int r)
   int len = p.topk;
   if (p.topk_length) len = min(len, __ldg(p.topk_length + ri.b));
   ri.len_main = max(len, 1);
+  ri.len_valid = max(len, 0);
   ri.ntm = (ri.len_main + kTileTokens - 1) / kTileTokens;
   int el = 0;
   if (p.extra_kv) {

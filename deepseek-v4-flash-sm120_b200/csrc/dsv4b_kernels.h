@@ -21,6 +21,13 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
 
 int decode_smem_bytes(int layout);
 
+// Sparse prefill (csrc/sparse_prefill.cu, csrc/sparse_decode_sm100a.cu):
+// the one-part-per-token schedule, then the decode kernel's bf16 layout.
+cudaError_t launch_sparse_prefill(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                                  const int32_t* num_splits, int* err, cudaStream_t stream);
+cudaError_t run_sparse_prefill(const dsv4b_decode_params& p, dsv4b_sched_meta* sched, int32_t* num_splits,
+                               int* err, cudaStream_t stream);
+
 // Test hook: whether the decode kernel's producers withhold their first
 // Q^T arrival on the current device (stall != 0), so that a wait runs out.
 cudaError_t set_decode_test_stall(int stall);

@@ -433,6 +433,134 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   }
 }
 
+// ------------------------------------------------------------- prefill producer
+// Sparse prefill (bf16 KV rows): nothing to dequantise, the producers copy
+// each row's 16-byte units into the swizzled chunk slots.  Same mapping as
+// the decode gather (warp w: rows 16w + 4k + (lane >> 3); lane q = lane & 7
+// takes columns 128m + 16q .. +15 of chunk pair m, i.e. 32 bytes), in two
+// register halves per tile (pairs 0-1, then pairs 2-3 and the 576-column
+// RoPE chunk): a thread's release arrive waits for its loads in flight, so
+// each half is loaded, landed and stored before the next is issued.  The
+// rows of the next tile are prefetched into L2 at the start of each tile.
+// Invalid positions are copied as zeros; the softmax leaves them out.
+template <int L>
+__device__ void run_producer_bf16(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
+                                  uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
+  using LT = LayoutT<L>;
+  constexpr int NCH = LT::kChunks;
+  const int ptid = threadIdx.x;
+  const int w = ptid >> 5, lane = ptid & 31;
+  const int q = lane & 7;
+  const int row0 = 16 * w + (lane >> 3);
+  volatile int* abort_flag = &M.abort;
+  const bool withhold_first_q = ptid == 0 && g_decode_test_stall != 0;
+
+  TileCursor cur = cursor_begin(p, sm);
+  if (!cur.valid) return;
+
+  auto issue_q = [&](const TileCursor& c) {
+    const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) + (int64_t)c.ri.b * p.stride_q_b +
+                              (int64_t)c.ri.s * p.stride_q_s;
+    for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
+      const int j = i / (NCH * 8);
+      const int rem = i - j * (NCH * 8);
+      const int ch = rem >> 3, u = rem & 7;
+      const int head = g * kHeadsPerCta + j;
+      const bool ok = head < p.h_q;
+      cp_async_16(q_s + ch * kQChunkBytes + sw128_off(j, u),
+                  qb + (ok ? (int64_t)head * p.stride_q_h + ch * 64 + u * 8 : 0), ok ? 16u : 0u);
+    }
+  };
+  // Address of tile row r, or nullptr for an invalid position.
+  auto row_ptr = [&](const TileCursor& c, int r) -> const uint8_t* {
+    if (!c.valid) return nullptr;
+    const TileSpan ts = tile_span(p, c);
+    const int lim = min(ts.npos, c.ri.len_valid - c.t * kTileTokens);
+    const int ix = r < lim ? __ldg(ts.idx + r) : -1;
+    return (ix >= 0 && ix < ts.num_tokens) ? ts.kv + (int64_t)ix * ts.stride_block : nullptr;
+  };
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  auto ld = [&](const uint8_t* s, int off) { return s ? ldg_nc_v4(s + off) : z; };
+  // Stores lane q's 16 columns of pair m of one row (units lo, hi) where
+  // the decode gather puts its dequantised pair (store_pair_fp8).
+  auto st_pair = [&](int m, int row, uint4 lo, uint4 hi) {
+    const uint32_t slot = slot_s + (2 * m + (q >> 2)) * kSlotBytes;
+    const int u = 2 * (q & 3);
+    const bool swap = (q & 4) != 0;
+    sts_v4(slot + sw128_off(row, u + (swap ? 1 : 0)), swap ? hi : lo);
+    sts_v4(slot + sw128_off(row, u + (swap ? 0 : 1)), swap ? lo : hi);
+  };
+
+  const uint8_t* src[kRowsPerThread];
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k) src[k] = row_ptr(cur, row0 + 4 * k);
+  issue_q(cur);
+  int tile = 0, seg = 0;
+  while (cur.valid) {
+    if (cur.t == cur.t_lo) {
+      // New query row: (re)load Q^T once the previous row's last QK^T is done.
+      if (seg > 0) {
+        if (!mbar_wait(&M.q_empty, (seg - 1) & 1, abort_flag, err)) break;
+        issue_q(cur);
+      }
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      if (seg != 0 || !withhold_first_q) mbar_arrive(&M.q_full);
+      ++seg;
+    }
+    const TileCursor nxt = cursor_next(p, sm, cur);
+    if (ptid < kTileTokens) {  // the next tile's rows into L2
+      const uint8_t* r = row_ptr(nxt, ptid);
+      if (r) prefetch_l2_bulk(r, (uint32_t)LT::kDqk * 2u);
+    }
+    const uint32_t par = (tile - 1) & 1;
+    bool ok = true;
+#pragma unroll
+    for (int h = 0; h < 2 && ok; ++h) {  // pairs 2h, 2h + 1
+      uint4 v[2][kRowsPerThread][2];
+#pragma unroll
+      for (int mm = 0; mm < 2; ++mm)
+#pragma unroll
+        for (int k = 0; k < kRowsPerThread; ++k) {
+          const int m = 2 * h + mm;
+          v[mm][k][0] = ld(src[k], 256 * m + 32 * q);
+          v[mm][k][1] = ld(src[k], 256 * m + 32 * q + 16);
+        }
+#pragma unroll
+      for (int mm = 0; mm < 2; ++mm) {
+        const int m = 2 * h + mm;
+        if (tile > 0 && !mbar_wait(&M.empty[m], par, abort_flag, err)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int k = 0; k < kRowsPerThread; ++k) st_pair(m, row0 + 4 * k, v[mm][k][0], v[mm][k][1]);
+        fence_proxy_async_smem();
+        mbar_arrive(&M.full[2 * m]);
+        mbar_arrive(&M.full[2 * m + 1]);
+      }
+    }
+    if (!ok) break;
+    if constexpr (LT::kPInRopeSlot) {
+      // RoPE chunk (columns 512..575; its slot holds P^T during PV)
+      uint4 rp[kRowsPerThread];
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k) rp[k] = ld(src[k], 1024 + 16 * q);
+      if (tile > 0 && !mbar_wait(&M.empty[4], par, abort_flag, err)) break;
+      const uint32_t slot = slot_s + (NCH - 1) * kSlotBytes;
+#pragma unroll
+      for (int k = 0; k < kRowsPerThread; ++k) sts_v4(slot + sw128_off(row0 + 4 * k, q), rp[k]);
+      fence_proxy_async_smem();
+      mbar_arrive(&M.full[NCH - 1]);
+    }
+#pragma unroll
+    for (int k = 0; k < kRowsPerThread; ++k) src[k] = row_ptr(nxt, row0 + 4 * k);
+    cur = nxt;
+    ++tile;
+  }
+  cp_async_wait_all();  // no copy may land after the CTA exits
+}
+
 // ------------------------------------------------------------- MMA issuer
 // One thread (lane 0 of the first softmax warp) issues every tcgen05.mma,
 // between that warp's softmax passes: QK^T of tile t+1 follows PV of tile
@@ -542,10 +670,17 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
     const int head = g * kHeadsPerCta + st;
     float lse = (m_run + log2f(l)) * kLn2;
     float scale = 1.0f / l;
+    const bool empty = p.prefill && !(l > 0.0f);  // no valid position (prefill)
+    if (empty) {  // FlashMLA sparse prefill: lse = +inf, max_logits = -inf, output 0
+      lse = INFINITY;
+      scale = 0.0f;
+    }
     if (head < p.h_q) {
       if (final_out) {
-        if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, scale);
+        if (p.attn_sink && !empty) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, scale);
         p.lse[((int64_t)cur.ri.b * p.h_q + head) * p.s_q + cur.ri.s] = lse;
+        if (p.max_logits)
+          p.max_logits[((int64_t)cur.ri.b * p.s_q + cur.ri.s) * p.h_q + head] = empty ? -INFINITY : m_run * kLn2;
       } else {
         lse_accum[(int64_t)split * p.h_q + head] = lse;
       }
@@ -622,7 +757,7 @@ __device__ __forceinline__ void fill_ones(Misc& M, int st) {
 // rose by more than 2^8 after the row's first tile, the rescale of that
 // head's O and row-sum columns in TMEM.
 __device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, bool seg_first,
-                                                 float& m_run, Misc& M) {
+                                                 float& m_run, Misc& M, float thr) {
   const int st = threadIdx.x - kProducerThreads;
   const int q = st >> 5, lane = st & 31;
   {
@@ -643,7 +778,7 @@ __device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, b
     float m_new = m_old, alpha = 1.0f;
     if (m_old == -INFINITY) {
       m_new = mt;
-    } else if (mt > m_old + kRescaleThreshold) {
+    } else if (mt > m_old + thr) {
       m_new = mt;
       alpha = fast_exp2(m_old - m_new);
       resc = true;
@@ -673,7 +808,7 @@ __device__ __forceinline__ void softmax_max_path(uint32_t tl, float row_scale, b
 // shared memory.  Returns whether any of this row's logits exceeds its
 // head's stabiliser by more than 2^8 (the P just written is then redone).
 __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uint32_t p_s,
-                                               const Misc& M) {
+                                               const Misc& M, float thr) {
   const int st = threadIdx.x - kProducerThreads;
   bool exceed = false;
   float sa[64];
@@ -690,8 +825,8 @@ __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uin
       const float x1 = fmaf(sv[4 * j4 + 1], row_scale, -mu.y);
       const float x2 = fmaf(sv[4 * j4 + 2], row_scale, -mu.z);
       const float x3 = fmaf(sv[4 * j4 + 3], row_scale, -mu.w);
-      exceed |= (fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)) > kRescaleThreshold);
       const bool live = row_scale != 0.0f;
+      exceed |= live && (fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)) > thr);
       pk[2 * j4] = pack_bf16(live ? fast_exp2(x0) : 0.0f, live ? fast_exp2(x1) : 0.0f);
       pk[2 * j4 + 1] = pack_bf16(live ? fast_exp2(x2) : 0.0f, live ? fast_exp2(x3) : 0.0f);
     }
@@ -740,6 +875,9 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
   MmaState ms;
   const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
   const float scale_log2 = p.sm_scale * kLog2e;
+  // Prefill reports the exact max logit: any growth of a head's max then
+  // takes the stabiliser path (threshold 0), so m_run is the running max.
+  const float thr = p.prefill ? 0.0f : kRescaleThreshold;
   volatile int* abort_flag = &M.abort;
 
   TileCursor cur = cursor_begin(p, sm);
@@ -757,7 +895,15 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     const bool seg_first = cur.t == cur.t_lo;
     const bool seg_last = cur.t + 1 == cur.t_hi;
     if (seg_first) m_run = -INFINITY;
-    const float row_scale = st < tile_span(p, cur).npos ? scale_log2 : 0.0f;  // 0 marks padding rows
+    // 0 marks a row left out of the softmax: padding past the row's length,
+    // and in prefill mode every invalid position (index < 0, >= the number
+    // of KV rows, or past topk_length), which FlashMLA masks out.
+    float row_scale = st < tile_span(p, cur).npos ? scale_log2 : 0.0f;
+    if (p.prefill) {
+      const TileSpan ts = tile_span(p, cur);
+      const int ix = st < ts.npos ? __ldg(ts.idx + st) : -1;  // prefill has no extra (SWA) tiles
+      if (st >= cur.ri.len_valid - cur.t * kTileTokens || ix < 0 || ix >= ts.num_tokens) row_scale = 0.0f;
+    }
 
     // On a failed wait the thread still runs this tile's softmax pass on
     // whatever TMEM holds (harmless) so that the group's vote below, which
@@ -775,15 +921,15 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
     // padding rows included.)
     if (seg_first) {
       if (!group_ok(s_ok)) return;
-      softmax_max_path(tl, row_scale, true, m_run, M);
-      softmax_p_pass(tl, row_scale, p_s, M);
+      softmax_max_path(tl, row_scale, true, m_run, M, thr);
+      softmax_p_pass(tl, row_scale, p_s, M, thr);
     } else {
-      const bool exceed = softmax_p_pass(tl, row_scale, p_s, M);
+      const bool exceed = softmax_p_pass(tl, row_scale, p_s, M, thr);
       __syncwarp();
       if (named_bar_or(1, kSoftmaxThreads, exceed || !s_ok)) {
         if (!group_ok(s_ok)) return;
-        softmax_max_path(tl, row_scale, false, m_run, M);
-        softmax_p_pass(tl, row_scale, p_s, M);
+        softmax_max_path(tl, row_scale, false, m_run, M, thr);
+        softmax_p_pass(tl, row_scale, p_s, M, thr);
       }
     }
     tc_wait_st();
@@ -1026,7 +1172,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = M.tmem_base;
 
   if (warp < kProducerWarps) {
-    run_producer<L>(p, sm, g, q_s, slot_s, M, err);
+    if constexpr (is_bf16_layout(L)) {
+      run_producer_bf16<L>(p, sm, g, q_s, slot_s, M, err);
+    } else {
+      run_producer<L>(p, sm, g, q_s, slot_s, M, err);
+    }
     cp_async_wait_all();  // an aborted producer may still have Q^T copies in flight
   } else {
     run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, q_s, slot_s, p_s, tmem, M, err, cluster_c);
@@ -1136,6 +1286,22 @@ cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_m
                             c > 1 ? c : 1);
 }
 
+// Sparse prefill: one CTA per (query token, 64-head group), no split, no
+// cluster (every row ends in the CTA's own epilogue).
+template <int L>
+cudaError_t launch_prefill_impl(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                                const int32_t* num_splits, int* err, cudaStream_t stream) {
+  cudaError_t e = set_smem_attr<L>();
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.b * p.s_q, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = SmemPlan<L>::kBytes;
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, sparse_decode_kernel<L>, p, sched, num_splits, (float*)nullptr,
+                            (float*)nullptr, err, 1);
+}
+
 }  // namespace
 
 // Cluster size of the plan for this batch; 1 = no cluster (split partials
@@ -1177,6 +1343,13 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
                                                 err, stream);
   return launch_decode_impl<DSV4B_LAYOUT_MODEL1>(p, sched, num_splits, num_sm_parts, lse_accum, o_accum,
                                                  err, stream);
+}
+
+cudaError_t launch_sparse_prefill(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
+                                  const int32_t* num_splits, int* err, cudaStream_t stream) {
+  if (p.layout == DSV4B_LAYOUT_BF16_576)
+    return launch_prefill_impl<DSV4B_LAYOUT_BF16_576>(p, sched, num_splits, err, stream);
+  return launch_prefill_impl<DSV4B_LAYOUT_BF16_512>(p, sched, num_splits, err, stream);
 }
 
 #ifdef DSV4B_TRACE

@@ -3,8 +3,9 @@
 Drop-in for the reference package's public surface
 (deepseek_v4_kernel/__init__.py:1-7): ``sparse_decode_fwd`` and
 ``patch_flash_mla``; plus the FlashMLA-compatible interface functions,
-the KV-cache writers that produce the FP8 pages (``cache_ops``) and the
-indexer logits that produce ``indices`` (``indexer``).
+the KV-cache writers that produce the FP8 pages (``cache_ops``), the
+indexer logits that produce ``indices`` (``indexer``) and the sparse
+prefill ``flash_mla_sparse_fwd`` (``prefill``).
 
 The public names are resolved on first use (PEP 562), so importing a
 host-only submodule such as ``deepseek_v4_kernel.kvcache`` or
@@ -25,6 +26,7 @@ _EXPORTS = {
     "fp8_paged_mqa_logits": ("indexer", "fp8_paged_mqa_logits"),
     "get_paged_mqa_logits_metadata": ("indexer", "get_paged_mqa_logits_metadata"),
     "FlashMLASchedMeta": ("interface", "FlashMLASchedMeta"),
+    "flash_mla_sparse_fwd": ("prefill", "flash_mla_sparse_fwd"),
     "flash_mla_with_kvcache": ("interface", "flash_mla_with_kvcache"),
     "get_mla_metadata": ("interface", "get_mla_metadata"),
     "gather_dequant": ("ops", "gather_dequant"),

@@ -13,6 +13,8 @@ LIB_PATH = os.environ.get("DSV4B_LIBRARY", os.path.join(_HERE, "libdsv4b.so"))
 
 LAYOUT_V32 = 0
 LAYOUT_MODEL1 = 1
+LAYOUT_BF16_576 = 2   # sparse prefill (bf16 KV rows)
+LAYOUT_BF16_512 = 3
 
 STATUS = {
     0: "DSV4B_OK",
@@ -34,7 +36,7 @@ EXPORTED = (
     "dsv4b_plan_cluster_size", "dsv4b_kv_cache_write",
     "dsv4b_kv_cache_write_status", "dsv4b_kv_write_selftest",
     "dsv4b_mqa_logits_metadata", "dsv4b_fp8_paged_mqa_logits", "dsv4b_mqa_logits_status",
-    "dsv4b_set_test_stall",
+    "dsv4b_set_test_stall", "dsv4b_prefill_workspace_bytes", "dsv4b_sparse_prefill",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -72,6 +74,7 @@ class DecodeParams(ctypes.Structure):
         ("extra_topk_length", _vp),
         ("out", _vp), ("stride_o_b", _i64), ("stride_o_s", _i64), ("stride_o_h", _i64),
         ("lse", _vp),
+        ("prefill", _i32), ("max_logits", _vp),
     ]
 
 
@@ -106,6 +109,9 @@ def _load():
     lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]
     lib.dsv4b_read_kernel_status.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_set_test_stall.argtypes = [ctypes.c_int]
+    lib.dsv4b_prefill_workspace_bytes.restype = ctypes.c_size_t
+    lib.dsv4b_prefill_workspace_bytes.argtypes = [ctypes.c_int]
+    lib.dsv4b_sparse_prefill.argtypes = [P, _vp, ctypes.c_size_t, _vp]
     return lib
 
 

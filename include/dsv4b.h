@@ -48,7 +48,12 @@ typedef enum dsv4b_layout {
   /* DeepSeek-V4-Flash: d_qk = d_v = 512; per page P x 576 B
    * [448 x e4m3 | 64 x bf16 RoPE] rows, then P x 8 B UE8M0 scales
    * (tests/reference.py:7-19). */
-  DSV4B_LAYOUT_MODEL1 = 1
+  DSV4B_LAYOUT_MODEL1 = 1,
+  /* Sparse prefill only (dsv4b_sparse_prefill): a bf16 [s_kv, d_qk] KV
+   * tensor, row stride stride_kv_block bytes, d_qk = 576 (V3.2 latent +
+   * RoPE; V = the first 512 columns) or 512 (V4; V = the whole row). */
+  DSV4B_LAYOUT_BF16_576 = 2,
+  DSV4B_LAYOUT_BF16_512 = 3
 } dsv4b_layout;
 
 /* One record per SM part, 32 bytes, field order of the reference's
@@ -100,6 +105,10 @@ typedef struct dsv4b_decode_params {
   void* out;                 /* bf16 [b, s_q, h_q, d_v] */
   int64_t stride_o_b, stride_o_s, stride_o_h;
   float* lse;                /* fp32 [b, h_q, s_q], contiguous */
+
+  /* Sparse prefill (dsv4b_sparse_prefill) only; 0 / NULL for decode. */
+  int32_t prefill;           /* 1: FlashMLA sparse-prefill semantics (see there) */
+  float* max_logits;         /* fp32 [b, h_q] (s_q = 1) or NULL */
 } dsv4b_decode_params;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -334,6 +343,33 @@ DSV4B_API int dsv4b_sparse_decode_noalloc(const dsv4b_decode_params* p,
                                           const dsv4b_sched_meta* sched_meta,
                                           const int32_t* num_splits, int num_sm_parts,
                                           void* stream);
+
+/* Bytes of device workspace dsv4b_sparse_prefill needs for `rows` query
+ * tokens (its tile schedule and the kernel status word). */
+DSV4B_API size_t dsv4b_prefill_workspace_bytes(int rows);
+
+/* Sparse attention prefill, FlashMLA's flash_mla_sparse_fwd
+ * (vLLM flash_mla_interface.py:180-217; the reference has no prefill: its
+ * kernel flattens s_q into the batch, csrc/sm120/decode/
+ * sparse_decode_kernel.cuh:38-40).  Each of the b query tokens (s_q = 1)
+ * attends, with all h_q heads, to the top-k rows of one bf16 KV tensor:
+ *   layout   DSV4B_LAYOUT_BF16_576 or DSV4B_LAYOUT_BF16_512 (d_qk 576/512);
+ *   kv       bf16 [num_blocks = s_kv rows, d_qk], page_block_size = 1,
+ *            stride_kv_block = row stride in bytes (multiple of 16);
+ *   indices  [b, topk] row numbers (stride_idx_b); -1 or >= s_kv: none;
+ *   topk_length [b] or NULL: only the first topk_length[i] indices count;
+ *   attn_sink [h_q] or NULL: the output (not lse / max_logits) is scaled by
+ *            exp(lse) / (exp(lse) + exp(sink)); lse_includes_sink must be 0;
+ *   prefill = 1; max_logits fp32 [b, h_q] or NULL; lse fp32 [b, h_q].
+ * Invalid positions are left out of the softmax (not zero rows, unlike
+ * decode).  lse is the natural-log log-sum-exp of sm_scale * q.k over the
+ * valid positions, max_logits their maximum; a token with no valid
+ * position gets lse = +inf, max_logits = -inf and a zero output (FlashMLA's
+ * conventions, checked against vLLM 0.22's kernel on B200).  Every token is
+ * one CTA per 64 heads (no split-KV); extra_kv is not supported.  Status
+ * word: dsv4b_read_kernel_status on the same workspace. */
+DSV4B_API int dsv4b_sparse_prefill(const dsv4b_decode_params* p, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
