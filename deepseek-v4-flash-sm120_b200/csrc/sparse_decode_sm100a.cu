@@ -973,9 +973,11 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
 // sink epilogue (tests/reference.py:124-129), lse = (M + log2 L) ln 2.
 // Rank j owns dims [j*512/C, (j+1)*512/C): every other rank stores its
 // weighted O for those dims into rank j's K-slot region (free once every
-// rank's PV is done) through distributed shared memory, as fp32
-// [sender][head quad][dim][4 heads], so a warp's 32 consecutive dims
-// write and read 512 contiguous bytes; rank j adds its own part from TMEM
+// rank's PV is done) through distributed shared memory, as bf16
+// [sender][head octet][dim][8 heads] (the weighted partial rounded once to
+// bf16; distributed shared memory runs at about 30 GB/s per SM, so the
+// bytes sent set the merge's floor), so a warp's 32 consecutive dims write
+// and read 512 contiguous bytes; rank j adds its own fp32 part from TMEM
 // and writes bf16.
 // Every thread of the CTA calls this; all waits before it are bounded, so
 // every CTA of the cluster reaches both cluster barriers.
@@ -985,7 +987,7 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
   const int st = threadIdx.x - kProducerThreads;
   const uint32_t self = cluster_ctarank();
   const int D = kDv / C;
-  const uint32_t blk_bytes = (uint32_t)D * 256u;  // one sender block: D dims x 64 heads x fp32
+  const uint32_t blk_bytes = (uint32_t)D * 128u;  // one sender block: D dims x 64 heads x bf16
   const uint32_t tl = tmem + ((uint32_t)((st >> 5) * 32) << 16);
   const int row = blockIdx.x / C;
   const int rb = row / p.s_q, rs = row - rb * p.s_q;
@@ -1042,11 +1044,18 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
         tmem_ld64(tl + kColO + 64 * m, ov);
         tc_wait_ld();
         if (owner != (int)self) {
+          // weighted O of 8 heads per 16-byte store, rounded to bf16: half
+          // the distributed-shared-memory bytes of fp32 (the merge's floor)
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const float4 w4 = *reinterpret_cast<const float4*>(&M.scale_o[4 * u]);
-            dsmem_st_v4(dst + (uint32_t)u * (uint32_t)D * 16u, ov[4 * u] * w4.x, ov[4 * u + 1] * w4.y,
-                        ov[4 * u + 2] * w4.z, ov[4 * u + 3] * w4.w);
+          for (int u = 0; u < 8; ++u) {
+            const float4 wa = *reinterpret_cast<const float4*>(&M.scale_o[8 * u]);
+            const float4 wb = *reinterpret_cast<const float4*>(&M.scale_o[8 * u + 4]);
+            const float* o8 = ov + 8 * u;
+            dsmem_st_v4(dst + (uint32_t)u * (uint32_t)D * 16u,
+                        __uint_as_float(pack_bf16(o8[0] * wa.x, o8[1] * wa.y)),
+                        __uint_as_float(pack_bf16(o8[2] * wa.z, o8[3] * wa.w)),
+                        __uint_as_float(pack_bf16(o8[4] * wb.x, o8[5] * wb.y)),
+                        __uint_as_float(pack_bf16(o8[6] * wb.z, o8[7] * wb.w)));
           }
         }
       }
@@ -1082,16 +1091,17 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
           for (int i = 0; i < C; ++i) {
             if (i == (int)self || !((live >> i) & 1u)) continue;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t u = (uint32_t)(8 * hf + 4 * c + k);
-              float4 v;
-              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                           : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+            for (int k = 0; k < 2; ++k) {  // 8 bf16 heads per 16-byte unit
+              const uint32_t u = (uint32_t)(4 * hf + 2 * c + k);
+              uint32_t v[4];
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                            : "r"(recv_s + (uint32_t)i * blk_bytes + (u * (uint32_t)D + (uint32_t)dl) * 16u));
-              acc[4 * k] += v.x;
-              acc[4 * k + 1] += v.y;
-              acc[4 * k + 2] += v.z;
-              acc[4 * k + 3] += v.w;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                acc[8 * k + 2 * e] += __uint_as_float(v[e] << 16);
+                acc[8 * k + 2 * e + 1] += __uint_as_float(v[e] & 0xFFFF0000u);
+              }
             }
           }
 #pragma unroll
