@@ -2,7 +2,9 @@
 // library; the public surface is include/dsv4b.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include "dsv4b.h"
 
@@ -20,6 +22,9 @@ cudaError_t launch_sparse_decode(const dsv4b_decode_params& p, const dsv4b_sched
                                  float* o_accum, int* err, cudaStream_t stream);
 
 int decode_smem_bytes(int layout);
+
+// cuTensorMapEncodeTiled from the driver (csrc/mqa_logits.cu).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 
 // Sparse prefill (csrc/sparse_prefill.cu, csrc/sparse_decode_sm100a.cu):
 // the one-part-per-token schedule, then the decode kernel's bf16 layout.

@@ -87,6 +87,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// As above with relaxed semantics: the arrive neither waits for nor orders
+// the thread's earlier memory operations.  For a barrier that only counts
+// TMA bytes, so that it does not stall on the thread's own loads in flight.
+__device__ __forceinline__ void mbar_arrive_expect_tx_relaxed(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.relaxed.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
 // Untiled bulk copy of `bytes` from global memory to this CTA's shared
 // memory (both addresses 16-byte aligned, bytes a multiple of 16); its
 // completion is counted as transaction bytes on `bar`.  No multicast.
@@ -302,6 +311,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t saddr, const void* tmap, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           saddr),
       "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t saddr, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(saddr),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t saddr, const void* tmap, int c0, int c1, int c2,

@@ -55,6 +55,20 @@ __device__ int g_mqa_status;  // kErr* bits of the logits kernel on this device
 // CTA withholds its first arrival, so the producer's first wait runs out.
 __device__ int g_mqa_test_stall = 0;
 
+// cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency);
+// nullptr if the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
 namespace {
 
 constexpr int kTileTok = 128;
@@ -508,18 +522,6 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
 }
 
 template <int N>

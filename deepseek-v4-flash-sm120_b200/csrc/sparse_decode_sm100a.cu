@@ -125,6 +125,7 @@ struct Misc {
   int abort;
   uint32_t sink_word;  // target of the producers' load-completion fold
   uint32_t cl_live;    // cluster epilogue: bit i = cluster rank i holds a partial
+  int q_loads;         // Q^T loads issued (thread 0); the abort path waits for the last
   alignas(16) float red[4][64];
   alignas(16) float m_use[64];    // read as float4
   alignas(16) float alpha[64];
@@ -167,6 +168,23 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 template <int L>
 __device__ __forceinline__ int empty_of(int c) {
   return (LayoutT<L>::kPInRopeSlot && c == LayoutT<L>::kChunks - 1) ? 4 : (c >> 1);
+}
+
+// ------------------------------------------------------------- Q^T load
+// Q^T of query row (b, s), head group g: NCH TMA tile loads (64 columns x
+// 64 heads, SWIZZLE_128B, straight into the chunk's 1024-byte-aligned
+// slot) from the 4-D q tensor map [b][s][h][d_qk], completing on q_full.
+// Issued by one thread: a TMA load bypasses the load/store path the row
+// gather saturates (a cp.async Q^T load shared it and delayed the first
+// tile by ~2 us).  Heads past h_q read as zeros (out of the tensor).
+template <int NCH>
+__device__ __forceinline__ void load_q_tma(const CUtensorMap* q_map, uint32_t q_s, int g, const TileCursor& c,
+                                           Misc& M) {
+  mbar_arrive_expect_tx_relaxed(&M.q_full, NCH * kQChunkBytes);
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch)
+    tma_load_4d(q_s + ch * kQChunkBytes, q_map, ch * 64, g * kHeadsPerCta, c.ri.s, c.ri.b, &M.q_full);
+  ++M.q_loads;
 }
 
 // ------------------------------------------------------------- producers
@@ -290,7 +308,7 @@ __device__ __forceinline__ void store_pair_fp8(uint32_t slot_s, int m, int row, 
 
 template <int L>
 __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
-                             uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
+                             uint32_t q_s, uint32_t slot_s, Misc& M, int* err, const CUtensorMap* q_map) {
   using LT = LayoutT<L>;
   constexpr int NCH = LT::kChunks;
   const int ptid = threadIdx.x;
@@ -302,25 +320,11 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   if (!cur.valid) return;
   TileCursor nxt = cursor_next(p, sm, cur);
 
-  // Q^T of a query row: 64 heads x d_qk bf16 by cp.async into SW128 chunks.
-  auto issue_q = [&](const TileCursor& c) {
-    const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) +
-                              (int64_t)c.ri.b * p.stride_q_b + (int64_t)c.ri.s * p.stride_q_s;
-    for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
-      const int j = i / (NCH * 8);
-      const int rem = i - j * (NCH * 8);
-      const int ch = rem >> 3, u = rem & 7;
-      const int head = g * kHeadsPerCta + j;
-      const bool ok = head < p.h_q;
-      cp_async_16(q_s + ch * kQChunkBytes + sw128_off(j, u),
-                  qb + (ok ? (int64_t)head * p.stride_q_h + ch * 64 + u * 8 : 0), ok ? 16u : 0u);
-    }
-  };
   // Test hook (read here, off the critical path: the load completes
   // while the first tile's rows are in flight).
   const bool withhold_first_q = ptid == 0 && g_decode_test_stall != 0;
   // The first row's Q^T is in flight together with the first tile's loads.
-  issue_q(cur);
+  if (ptid == 0 && !withhold_first_q) load_q_tma<NCH>(q_map, q_s, g, cur, M);
 
   ProdRegs<L> R;
   int idx[kRowsPerThread];
@@ -338,13 +342,10 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
   while (cur.valid) {
     if (cur.t == cur.t_lo) {
       // New query row: (re)load Q^T once the previous row's last QK^T is done.
-      if (seg_count > 0) {
+      if (seg_count > 0 && ptid == 0) {
         if (!mbar_wait(&M.q_empty, (seg_count - 1) & 1, abort_flag, err)) return;
-        issue_q(cur);
+        load_q_tma<NCH>(q_map, q_s, g, cur, M);
       }
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      if (seg_count != 0 || !withhold_first_q) mbar_arrive(&M.q_full);
       if (ptid == 0) DSV4B_TR_ROLE(0, 5, seg_count);
       ++seg_count;
     }
@@ -445,7 +446,7 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
 // Invalid positions are copied as zeros; the softmax leaves them out.
 template <int L>
 __device__ void run_producer_bf16(const dsv4b_decode_params& p, const dsv4b_sched_meta& sm, int g,
-                                  uint32_t q_s, uint32_t slot_s, Misc& M, int* err) {
+                                  uint32_t q_s, uint32_t slot_s, Misc& M, int* err, const CUtensorMap* q_map) {
   using LT = LayoutT<L>;
   constexpr int NCH = LT::kChunks;
   const int ptid = threadIdx.x;
@@ -458,19 +459,6 @@ __device__ void run_producer_bf16(const dsv4b_decode_params& p, const dsv4b_sche
   TileCursor cur = cursor_begin(p, sm);
   if (!cur.valid) return;
 
-  auto issue_q = [&](const TileCursor& c) {
-    const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(p.q) + (int64_t)c.ri.b * p.stride_q_b +
-                              (int64_t)c.ri.s * p.stride_q_s;
-    for (int i = ptid; i < kHeadsPerCta * NCH * 8; i += kProducerThreads) {
-      const int j = i / (NCH * 8);
-      const int rem = i - j * (NCH * 8);
-      const int ch = rem >> 3, u = rem & 7;
-      const int head = g * kHeadsPerCta + j;
-      const bool ok = head < p.h_q;
-      cp_async_16(q_s + ch * kQChunkBytes + sw128_off(j, u),
-                  qb + (ok ? (int64_t)head * p.stride_q_h + ch * 64 + u * 8 : 0), ok ? 16u : 0u);
-    }
-  };
   // Address of tile row r, or nullptr for an invalid position.
   auto row_ptr = [&](const TileCursor& c, int r) -> const uint8_t* {
     if (!c.valid) return nullptr;
@@ -494,18 +482,15 @@ __device__ void run_producer_bf16(const dsv4b_decode_params& p, const dsv4b_sche
   const uint8_t* src[kRowsPerThread];
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) src[k] = row_ptr(cur, row0 + 4 * k);
-  issue_q(cur);
+  if (ptid == 0 && !withhold_first_q) load_q_tma<NCH>(q_map, q_s, g, cur, M);
   int tile = 0, seg = 0;
   while (cur.valid) {
     if (cur.t == cur.t_lo) {
       // New query row: (re)load Q^T once the previous row's last QK^T is done.
-      if (seg > 0) {
+      if (seg > 0 && ptid == 0) {
         if (!mbar_wait(&M.q_empty, (seg - 1) & 1, abort_flag, err)) break;
-        issue_q(cur);
+        load_q_tma<NCH>(q_map, q_s, g, cur, M);
       }
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      if (seg != 0 || !withhold_first_q) mbar_arrive(&M.q_full);
       ++seg;
     }
     const TileCursor nxt = cursor_next(p, sm, cur);
@@ -1127,7 +1112,8 @@ template <int L>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_decode_kernel(const dsv4b_decode_params p, const dsv4b_sched_meta* __restrict__ sched,
                          const int32_t* __restrict__ num_splits, float* __restrict__ lse_accum,
-                         float* __restrict__ o_accum, int* __restrict__ err, int cluster_c) {
+                         float* __restrict__ o_accum, int* __restrict__ err, int cluster_c,
+                         const __grid_constant__ CUtensorMap q_map) {
   using SP = SmemPlan<L>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1150,7 +1136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = 0; e < 5; ++e) mbar_init(&M.empty[e], 1);
     mbar_init(&M.s_full, 1);
     mbar_init(&M.p_full, kSoftmaxThreads);
-    mbar_init(&M.q_full, kProducerThreads);
+    mbar_init(&M.q_full, 1);  // one arrive (+ the Q^T bytes) per load
+    M.q_loads = 0;
     mbar_init(&M.q_empty, 1);
     mbar_init(&M.o_full, 1);
     mbar_init(&M.drain, 1);
@@ -1183,11 +1170,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kProducerWarps) {
     if constexpr (is_bf16_layout(L)) {
-      run_producer_bf16<L>(p, sm, g, q_s, slot_s, M, err);
+      run_producer_bf16<L>(p, sm, g, q_s, slot_s, M, err, &q_map);
     } else {
-      run_producer<L>(p, sm, g, q_s, slot_s, M, err);
+      run_producer<L>(p, sm, g, q_s, slot_s, M, err, &q_map);
     }
-    cp_async_wait_all();  // an aborted producer may still have Q^T copies in flight
+    cp_async_wait_all();
+    if (threadIdx.x == 0 && M.abort && M.q_loads > 0) {
+      // aborted: the last Q^T load lands before the CTA's shared memory goes
+      // away (its barrier completes on its bytes alone; bounded wait)
+      const long long t0 = clock64();
+      while (!mbar_try_wait(smem_u32(&M.q_full), (M.q_loads - 1) & 1) && clock64() - t0 < 2000000) {
+      }
+    }
   } else {
     run_softmax<L>(p, sm, g, num_splits, lse_accum, o_accum, q_s, slot_s, p_s, tmem, M, err, cluster_c);
     if (warp == kMmaWarp) {
@@ -1272,12 +1266,35 @@ int clusters_resident(int c) {
   return cache[dev][k] - 1;
 }
 
+// 4-D TMA map of q, dims (innermost first) {d_qk, h_q, s_q, b}, box
+// {64, 64, 1, 1} with SWIZZLE_128B: one box = one Q^T chunk slot.  A size-1
+// dimension gets a nominal stride (its coordinate is always 0).
+template <int L>
+cudaError_t make_q_map(const dsv4b_decode_params& p, CUtensorMap* map) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t sh = (cuuint64_t)p.stride_q_h * 2;
+  const cuuint64_t ss = p.s_q > 1 ? (cuuint64_t)p.stride_q_s * 2 : sh * (cuuint64_t)p.h_q;
+  const cuuint64_t sb = p.b > 1 ? (cuuint64_t)p.stride_q_b * 2 : ss * (cuuint64_t)p.s_q;
+  const cuuint64_t dims[4] = {(cuuint64_t)LayoutT<L>::kDqk, (cuuint64_t)p.h_q, (cuuint64_t)p.s_q, (cuuint64_t)p.b};
+  const cuuint64_t strides[3] = {sh, ss, sb};
+  const cuuint32_t box[4] = {64u, (cuuint32_t)kHeadsPerCta, 1u, 1u};
+  const cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  if (enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(p.q), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
 template <int L>
 cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_meta* sched,
                                const int32_t* num_splits, int num_sm_parts, float* lse_accum,
                                float* o_accum, int* err, cudaStream_t stream) {
   cudaError_t e = set_smem_attr<L>();
   if (e != cudaSuccess) return e;
+  CUtensorMap q_map;
+  if ((e = make_q_map<L>(p, &q_map)) != cudaSuccess) return e;
   const int c = plan_cluster_size(p, num_sm_parts);
   const int groups = (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta;
   cudaLaunchConfig_t cfg = {};
@@ -1293,7 +1310,7 @@ cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_m
   cfg.attrs = &attr;
   cfg.numAttrs = c > 1 ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, sparse_decode_kernel<L>, p, sched, num_splits, lse_accum, o_accum, err,
-                            c > 1 ? c : 1);
+                            c > 1 ? c : 1, q_map);
 }
 
 // Sparse prefill: one CTA per (query token, 64-head group), no split, no
@@ -1303,13 +1320,15 @@ cudaError_t launch_prefill_impl(const dsv4b_decode_params& p, const dsv4b_sched_
                                 const int32_t* num_splits, int* err, cudaStream_t stream) {
   cudaError_t e = set_smem_attr<L>();
   if (e != cudaSuccess) return e;
+  CUtensorMap q_map;
+  if ((e = make_q_map<L>(p, &q_map)) != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.b * p.s_q, (p.h_q + kHeadsPerCta - 1) / kHeadsPerCta, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = SmemPlan<L>::kBytes;
   cfg.stream = stream;
   return cudaLaunchKernelEx(&cfg, sparse_decode_kernel<L>, p, sched, num_splits, (float*)nullptr,
-                            (float*)nullptr, err, 1);
+                            (float*)nullptr, err, 1, q_map);
 }
 
 }  // namespace
