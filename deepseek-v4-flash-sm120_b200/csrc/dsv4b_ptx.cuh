@@ -156,6 +156,12 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t cluster_saddr) {
   return v;
 }
 
+__device__ __forceinline__ float2 dsmem_ld_f32x2(uint32_t cluster_saddr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(cluster_saddr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void dsmem_st_v4(uint32_t cluster_saddr, float a, float b, float c, float d) {
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_saddr), "f"(a), "f"(b),
                "f"(c), "f"(d)

@@ -103,6 +103,9 @@ constexpr int kThreads = (kProducerWarps + kSoftmaxWarps) * 32;  // 384
 constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kMmaWarp = kProducerWarps;  // lane 0 of the first softmax warp issues the MMAs
+// Named barriers of the cluster merge: its 256 worker threads, then each
+// half's 128 (one staging tile per half).
+constexpr uint32_t kMergeBar = 3;
 
 constexpr int kQChunkBytes = kHeadsPerCta * 128;       // 8 KB
 constexpr int kSlotBytes = kTileTokens * 128;          // 16 KB
@@ -844,8 +847,13 @@ __device__ __forceinline__ bool softmax_p_pass(uint32_t tl, float row_scale, uin
   return exceed && row_scale != 0.0f;
 }
 
+// (m, l) of head j for the cluster merge, adjacent so that a peer reads
+// both with one distributed-shared-memory load (red[2..3]; the max-path
+// exchange rows are free once the row's last tile is done).
+__device__ __forceinline__ float2* merge_ml(Misc& M) { return reinterpret_cast<float2*>(&M.red[2][0]); }
+
 // Cluster plan: instead of the epilogue, publish this CTA's per-head
-// stabiliser (red[1]) and row sum (red[2]) for the cluster merge.
+// stabiliser and row sum (merge_ml) for the cluster merge.
 __device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& M) {
   const int st = threadIdx.x - kProducerThreads;
   if ((st >> 5) == 0) {
@@ -854,10 +862,10 @@ __device__ __forceinline__ void publish_partial(uint32_t tl, float m_run, Misc& 
     tc_wait_ld();
     if (st == 0) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) M.red[2][j] = lv[j];
+      for (int j = 0; j < 64; ++j) merge_ml(M)[j].y = lv[j];
     }
   }
-  if (st < 64) M.red[1][st] = m_run;
+  if (st < 64) merge_ml(M)[st].x = m_run;
 }
 
 // The softmax threads leave on a wait failure only all together: each
@@ -892,8 +900,7 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
   int tile_count = 0, seg_count = 0;
   float m_run = -INFINITY;  // stabiliser of head `st` (threads 0..63), log2 units
   if (cluster_c > 1 && !cur.valid && st < 64) {  // a cluster rank with no tiles
-    M.red[1][st] = -INFINITY;
-    M.red[2][st] = 0.0f;
+    merge_ml(M)[st] = make_float2(-INFINITY, 0.0f);
   }
   // MMA issue of the first tile; later tiles' QK^T follows the previous PV.
   bool mma_ok = true;  // lane 0 of warp kMmaWarp: false once an MMA-side wait gave up
@@ -975,8 +982,8 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
 }
 
 // Cluster merge of one query row over the C = cluster_c CTAs that split
-// it (cluster ranks 0..C-1; rank i holds m_i, l_i per head in red[1],
-// red[2] and its unnormalised O_i^T in TMEM).  With M = max_i m_i and
+// it (cluster ranks 0..C-1; rank i holds m_i, l_i per head in merge_ml
+// and its unnormalised O_i^T in TMEM).  With M = max_i m_i and
 // L = sum_i l_i 2^(m_i - M): out = sum_i (2^(m_i - M) / L) O_i, then the
 // sink epilogue (tests/reference.py:124-129), lse = (M + log2 L) ln 2.
 // Rank j owns dims [j*512/C, (j+1)*512/C): every other rank stores its
@@ -990,81 +997,92 @@ __device__ void run_softmax(const dsv4b_decode_params& p, const dsv4b_sched_meta
 // Every thread of the CTA calls this; all waits before it are bounded, so
 // every CTA of the cluster reaches both cluster barriers.
 __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uint32_t tmem,
-                                 uint32_t recv_s, Misc& M) {
+                                 uint32_t recv_s, uint8_t* qarea, Misc& M) {
   const bool softmax = threadIdx.x >= kProducerThreads && threadIdx.x < kProducerThreads + kSoftmaxThreads;
+  // The merge's data movement is latency-bound with one warp per SM
+  // sub-partition, so producer warps 0-3 (idle by now; they read the same
+  // TMEM lane quarters) take half of it: M-blocks 2-3 of the send and heads
+  // 32-63 of the output.
+  const bool helper = threadIdx.x < kSoftmaxThreads;
+  const bool worker = softmax || helper;
   const int st = threadIdx.x - kProducerThreads;
+  const int lane_row = softmax ? st : (int)threadIdx.x;  // TMEM lane = dim within an M-block
+  const int half = helper ? 1 : 0;
   const uint32_t self = cluster_ctarank();
   const int D = kDv / C;
   const uint32_t blk_bytes = (uint32_t)D * 128u;  // one sender block: D dims x 64 heads x bf16
-  const uint32_t tl = tmem + ((uint32_t)((st >> 5) * 32) << 16);
+  const uint32_t tl = tmem + ((uint32_t)((lane_row >> 5) * 32) << 16);
   const int row = blockIdx.x / C;
   const int rb = row / p.s_q, rs = row - rb * p.s_q;
 
   if (st == 0) DSV4B_TR_ROLE(2, 30, 0);
   cluster_sync_all();  // 1: every rank's (m, l) is published and its PV is done
   if (st == 0) DSV4B_TR_ROLE(2, 31, 0);
-  if (softmax) {
-    if (st < 64) {
-      float mi[8], li[8];
-      float mx = -INFINITY;
+  if (softmax && st < 64) {
+    float mi[8], li[8];
+    float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mi[i] = -INFINITY;
-        li[i] = 0.0f;
-        if (i < C) {
-          mi[i] = dsmem_ld_f32(dsmem_addr(smem_u32(&M.red[1][st]), i));
-          li[i] = dsmem_ld_f32(dsmem_addr(smem_u32(&M.red[2][st]), i));
-          if (li[i] > 0.0f) mx = fmaxf(mx, mi[i]);
-        }
+    for (int i = 0; i < 8; ++i) {
+      mi[i] = -INFINITY;
+      li[i] = 0.0f;
+      if (i < C) {
+        const float2 ml = dsmem_ld_f32x2(dsmem_addr(smem_u32(&merge_ml(M)[st]), i));
+        mi[i] = ml.x;
+        li[i] = ml.y;
       }
-      float l = 0.0f;
-      uint32_t live = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (li[i] > 0.0f) {
-          l += li[i] * fast_exp2(mi[i] - mx);
-          live |= 1u << i;
-        }
-      float w = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i == (int)self && li[i] > 0.0f) w = fast_exp2(mi[i] - mx) / l;
-      const int head = g * kHeadsPerCta + st;
-      float lse = (mx + log2f(l)) * kLn2;
-      if (head < p.h_q) {
-        if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, w);
-        if (self == 0) p.lse[((int64_t)rb * p.h_q + head) * p.s_q + rs] = lse;
-      } else {
-        w = 0.0f;
-      }
-      M.scale_o[st] = w;
-      if (st == 0) M.cl_live = live;
     }
-    named_bar_sync(1, kSoftmaxThreads);
-    const uint32_t live = M.cl_live;
-    if (live & (1u << self)) {
-#pragma unroll 1
-      for (int m = 0; m < 4; ++m) {
-        const int d = 128 * m + st;
-        const int owner = d / D, dl = d - owner * D;
-        const uint32_t dst = dsmem_addr(recv_s + self * blk_bytes + (uint32_t)dl * 16u, owner);
-        float ov[64];
-        tmem_ld64(tl + kColO + 64 * m, ov);
-        tc_wait_ld();
-        if (owner != (int)self) {
-          // weighted O of 8 heads per 16-byte store, rounded to bf16: half
-          // the distributed-shared-memory bytes of fp32 (the merge's floor)
+    // all C remote loads are issued above before any is used
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float4 wa = *reinterpret_cast<const float4*>(&M.scale_o[8 * u]);
-            const float4 wb = *reinterpret_cast<const float4*>(&M.scale_o[8 * u + 4]);
-            const float* o8 = ov + 8 * u;
-            dsmem_st_v4(dst + (uint32_t)u * (uint32_t)D * 16u,
-                        __uint_as_float(pack_bf16(o8[0] * wa.x, o8[1] * wa.y)),
-                        __uint_as_float(pack_bf16(o8[2] * wa.z, o8[3] * wa.w)),
-                        __uint_as_float(pack_bf16(o8[4] * wb.x, o8[5] * wb.y)),
-                        __uint_as_float(pack_bf16(o8[6] * wb.z, o8[7] * wb.w)));
-          }
+    for (int i = 0; i < 8; ++i)
+      if (li[i] > 0.0f) mx = fmaxf(mx, mi[i]);
+    float l = 0.0f;
+    uint32_t live = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (li[i] > 0.0f) {
+        l += li[i] * fast_exp2(mi[i] - mx);
+        live |= 1u << i;
+      }
+    float w = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i == (int)self && li[i] > 0.0f) w = fast_exp2(mi[i] - mx) / l;
+    const int head = g * kHeadsPerCta + st;
+    float lse = (mx + log2f(l)) * kLn2;
+    if (head < p.h_q) {
+      if (p.attn_sink) apply_sink(__ldg(p.attn_sink + head), p.lse_includes_sink, lse, w);
+      if (self == 0) p.lse[((int64_t)rb * p.h_q + head) * p.s_q + rs] = lse;
+    } else {
+      w = 0.0f;
+    }
+    M.scale_o[st] = w;
+    if (st == 0) M.cl_live = live;
+  }
+  if (st == 0) DSV4B_TR_ROLE(2, 35, 0);
+  if (worker) named_bar_sync(kMergeBar, 2 * kSoftmaxThreads);
+  if (st == 0) DSV4B_TR_ROLE(2, 36, 0);
+  if (worker && ((M.cl_live >> self) & 1u)) {
+#pragma unroll 1
+    for (int m = 2 * half; m < 2 * half + 2; ++m) {
+      const int d = 128 * m + lane_row;
+      const int owner = d / D, dl = d - owner * D;
+      const uint32_t dst = dsmem_addr(recv_s + self * blk_bytes + (uint32_t)dl * 16u, owner);
+      float ov[64];
+      tmem_ld64(tl + kColO + 64 * m, ov);
+      tc_wait_ld();
+      if (owner != (int)self) {
+        // weighted O of 8 heads per 16-byte store, rounded to bf16: half
+        // the distributed-shared-memory bytes of fp32
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 wa = *reinterpret_cast<const float4*>(&M.scale_o[8 * u]);
+          const float4 wb = *reinterpret_cast<const float4*>(&M.scale_o[8 * u + 4]);
+          const float* o8 = ov + 8 * u;
+          dsmem_st_v4(dst + (uint32_t)u * (uint32_t)D * 16u,
+                      __uint_as_float(pack_bf16(o8[0] * wa.x, o8[1] * wa.y)),
+                      __uint_as_float(pack_bf16(o8[2] * wa.z, o8[3] * wa.w)),
+                      __uint_as_float(pack_bf16(o8[4] * wb.x, o8[5] * wb.y)),
+                      __uint_as_float(pack_bf16(o8[6] * wb.z, o8[7] * wb.w)));
         }
       }
     }
@@ -1072,61 +1090,66 @@ __device__ void cluster_epilogue(const dsv4b_decode_params& p, int g, int C, uin
   if (st == 0) DSV4B_TR_ROLE(2, 32, 0);
   cluster_sync_all();  // 2: every rank's contribution has landed at its owner
   if (st == 0) DSV4B_TR_ROLE(2, 33, 0);
-  if (!softmax) return;
+  if (!worker) return;
   const uint32_t live = M.cl_live;
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)rb * p.stride_o_b +
                        (int64_t)rs * p.stride_o_s;
   const int lo = (int)self * D, hi = lo + D;
-  const int r = st >> 2, part = st & 3;
+  const bool own = (live >> self) & 1u;
+  // Dim d = 128 m + lane_row of each M-block in [lo, hi), heads 32*half ..
+  // +31: the own weighted part from TMEM, plus every other live rank's bf16
+  // part from the receive area (all loads issued before any is summed),
+  // then through this half's [32 heads][128 dims] bf16 staging tile (in the
+  // Q^T region, free after the last QK^T) so that the global stores are 16
+  // bytes and contiguous along dims.
+  __nv_bfloat16(*stage)[128] = reinterpret_cast<__nv_bfloat16(*)[128]>(qarea + half * 32 * 128 * 2);
+  const int r = lane_row >> 2, part = lane_row & 3;
+  // Every thread of the half runs every iteration and both barriers: with
+  // C = 8 (D = 64) only half of an M-block's dims belong to this rank.
 #pragma unroll 1
   for (int m = lo / 128; m * 128 < hi; ++m) {
-    const int d = 128 * m + st;
+    const int d = 128 * m + lane_row;
     const bool mine = d >= lo && d < hi;  // uniform per warp (D >= 64)
     const int dl = d - lo;
+    if (mine) {
+      float acc[32];
+      tmem_ld32(tl + kColO + 64 * m + 32 * half, acc);
+      tc_wait_ld();
+      if (st == 0) DSV4B_TR_ROLE(2, 38, m);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] = own ? acc[j] * M.scale_o[32 * half + j] : 0.0f;
 #pragma unroll 1
-    for (int hf = 0; hf < 2; ++hf) {
-      if (mine) {
-        float acc32[32];
-        tmem_ld32(tl + kColO + 64 * m + 32 * hf, acc32);
-        tc_wait_ld();
+      for (int i = 0; i < C; ++i) {
+        if (i == (int)self || !((live >> i) & 1u)) continue;
+        uint32_t v[4][4];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float* acc = acc32 + 16 * c;
-          const bool own = (live >> self) & 1u;
+        for (int u = 0; u < 4; ++u)  // 8 heads per 16-byte unit
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3])
+                       : "r"(recv_s + (uint32_t)i * blk_bytes +
+                             ((uint32_t)(4 * half + u) * (uint32_t)D + (uint32_t)dl) * 16u));
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = own ? acc[j] * M.scale_o[32 * hf + 16 * c + j] : 0.0f;
-#pragma unroll 1
-          for (int i = 0; i < C; ++i) {
-            if (i == (int)self || !((live >> i) & 1u)) continue;
+        for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {  // 8 bf16 heads per 16-byte unit
-              const uint32_t u = (uint32_t)(4 * hf + 2 * c + k);
-              uint32_t v[4];
-              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                           : "r"(recv_s + (uint32_t)i * blk_bytes + (u * (uint32_t)D + (uint32_t)dl) * 16u));
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                acc[8 * k + 2 * e] += __uint_as_float(v[e] << 16);
-                acc[8 * k + 2 * e + 1] += __uint_as_float(v[e] & 0xFFFF0000u);
-              }
-            }
+          for (int e = 0; e < 4; ++e) {
+            acc[8 * u + 2 * e] += __uint_as_float(v[u][e] << 16);
+            acc[8 * u + 2 * e + 1] += __uint_as_float(v[u][e] & 0xFFFF0000u);
           }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) M.stage[16 * c + j][st] = __float2bfloat16_rn(acc[j]);
-        }
       }
-      named_bar_sync(1, kSoftmaxThreads);
-      const int head = g * kHeadsPerCta + 32 * hf + r;
-      const int dq = 128 * m + 32 * part;
-      if (head < p.h_q && dq >= lo && dq < hi) {
-        uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)head * p.stride_o_h + dq);
-        const uint4* src = reinterpret_cast<const uint4*>(&M.stage[r][32 * part]);
+      if (st == 0) DSV4B_TR_ROLE(2, 39, m);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = src[k];
-      }
-      named_bar_sync(1, kSoftmaxThreads);
+      for (int j = 0; j < 32; ++j) stage[j][lane_row] = __float2bfloat16_rn(acc[j]);
     }
+    named_bar_sync(kMergeBar + 1 + half, kSoftmaxThreads);
+    const int head = g * kHeadsPerCta + 32 * half + r;
+    const int dq = 128 * m + 32 * part;
+    if (head < p.h_q && dq >= lo && dq < hi) {
+      uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)head * p.stride_o_h + dq);
+      const uint4* src = reinterpret_cast<const uint4*>(&stage[r][32 * part]);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) dst[q4] = src[q4];
+    }
+    named_bar_sync(kMergeBar + 1 + half, kSoftmaxThreads);
   }
   if (st == 0) DSV4B_TR_ROLE(2, 34, 0);
 }
@@ -1225,7 +1248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (cluster_c > 1) {
     tc_fence_after();
-    cluster_epilogue(p, g, cluster_c, tmem, slot_s, M);
+    cluster_epilogue(p, g, cluster_c, tmem, slot_s, base + SP::kQOff, M);
     tc_fence_before();
     __syncthreads();
   }
