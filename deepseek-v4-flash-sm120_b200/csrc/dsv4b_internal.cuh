@@ -220,26 +220,35 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t b) {
 
 // Two e4m3 (low byte first) -> two bf16 = RN_bf16(fp32(e4m3) * scale):
 // e4m3 -> f16 is exact, f16 -> f32 is exact, one fp32 RN multiply, one RN
-// round to bf16; the order of tests/reference.py:53-56.
-__device__ __forceinline__ uint32_t dq_pair(uint32_t two, float s) {
+// round to bf16; the order of tests/reference.py:53-56.  The scale comes
+// pre-packed as {s, s}, so the two fp32 multiplies are one packed f32x2
+// multiply (Blackwell; each lane an ordinary IEEE fp32 RN multiply).
+__device__ __forceinline__ uint32_t dq_pair2(uint32_t two, uint64_t ss) {
   const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
   __half2 h;
   *reinterpret_cast<__half2_raw*>(&h) = hr;
   const float2 f = __half22float2(h);
-  const __nv_bfloat162 o = __floats2bfloat162_rn(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
+  uint64_t a, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(f.x), "f"(f.y));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(ss));
+  float x, y;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(d));
+  const __nv_bfloat162 o = __floats2bfloat162_rn(x, y);
   return *reinterpret_cast<const uint32_t*>(&o);
 }
 
 // 16 e4m3 -> 16 bf16 (two 16-byte units), one scale.
 __device__ __forceinline__ void dq16(uint4 in, float s, uint4& lo, uint4& hi) {
-  lo.x = dq_pair(in.x & 0xFFFFu, s);
-  lo.y = dq_pair(in.x >> 16, s);
-  lo.z = dq_pair(in.y & 0xFFFFu, s);
-  lo.w = dq_pair(in.y >> 16, s);
-  hi.x = dq_pair(in.z & 0xFFFFu, s);
-  hi.y = dq_pair(in.z >> 16, s);
-  hi.z = dq_pair(in.w & 0xFFFFu, s);
-  hi.w = dq_pair(in.w >> 16, s);
+  uint64_t ss;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
+  lo.x = dq_pair2(in.x & 0xFFFFu, ss);
+  lo.y = dq_pair2(in.x >> 16, ss);
+  lo.z = dq_pair2(in.y & 0xFFFFu, ss);
+  lo.w = dq_pair2(in.y >> 16, ss);
+  hi.x = dq_pair2(in.z & 0xFFFFu, ss);
+  hi.y = dq_pair2(in.z >> 16, ss);
+  hi.z = dq_pair2(in.w & 0xFFFFu, ss);
+  hi.w = dq_pair2(in.w >> 16, ss);
 }
 
 // Scale of FP8 chunk c (64 columns) of a row, from the raw scale bytes.
