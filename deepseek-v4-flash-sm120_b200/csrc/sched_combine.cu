@@ -82,6 +82,9 @@ __global__ void __launch_bounds__(kSchedThreads)
   // scratch first: its base stays 16-byte aligned whatever R is, so the
   // 32-entry reductions over it may be read as vectors.
   extern __shared__ __align__(16) int sh[];
+  // The decode grid that follows may launch now (its CTAs set up on-chip
+  // state, then wait in griddepcontrol.wait for this grid to complete).
+  asm volatile("griddepcontrol.launch_dependents;");
   const int R = p.b * p.s_q;
   int* scratch = sh;                // [32]
   int* tile_off = sh + 32;          // [R + 1]

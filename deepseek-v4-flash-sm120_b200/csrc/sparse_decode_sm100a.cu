@@ -726,29 +726,20 @@ __device__ __forceinline__ void epilogue(const dsv4b_decode_params& p, const dsv
       named_bar_sync(1, kSoftmaxThreads);
     }
   } else {
-    // fp32 partial [split][h_q][512] through the same staging tile (16 heads x
-    // 128 dims per round): each row goes out as full 128-byte segments.
-    float* stage = reinterpret_cast<float*>(&M.stage[0][0]);  // [16][128] fp32
-    const int r = st >> 3, part = st & 7;
+    // fp32 partial [split][h_q][512]: thread st holds dim 128 m + st of each
+    // M-block for all 64 heads, so one store per head is already coalesced
+    // (a warp's 32 adjacent dims write 128 contiguous bytes); no staging.
+    const int hmax = min(kHeadsPerCta, p.h_q - g * kHeadsPerCta);
+    float* dst = o_accum + ((int64_t)split * p.h_q + g * kHeadsPerCta) * kDv;
 #pragma unroll 1
-    for (int m = 0; m < 4; ++m) {  // 4 M-blocks, each in 4 rounds of 16 heads
+    for (int m = 0; m < 4; ++m) {
       float ov[64];
       tmem_ld64(tl + kColO + 64 * m, ov);
       tc_wait_ld();
+      const int d = 128 * m + st;
 #pragma unroll
-      for (int hg = 0; hg < 4; ++hg) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) stage[j * 128 + st] = ov[16 * hg + j] * M.scale_o[16 * hg + j];
-        named_bar_sync(1, kSoftmaxThreads);
-        const int head = g * kHeadsPerCta + 16 * hg + r;
-        if (head < p.h_q) {
-          float4* dst = reinterpret_cast<float4*>(o_accum + ((int64_t)split * p.h_q + head) * kDv + 128 * m);
-          const float4* src = reinterpret_cast<const float4*>(stage + r * 128);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) dst[8 * k + part] = src[8 * k + part];
-        }
-        named_bar_sync(1, kSoftmaxThreads);
-      }
+      for (int j = 0; j < 64; ++j)
+        if (j < hmax) dst[(int64_t)j * kDv + d] = ov[j] * M.scale_o[j];
     }
   }
 }
@@ -1174,7 +1165,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // A dependent combine launch may be scheduled now; it waits in-kernel
   // for this grid's completion (griddepcontrol.wait).
   asm volatile("griddepcontrol.launch_dependents;");
-  const dsv4b_sched_meta sm = sched[blockIdx.x];
   const int g = blockIdx.y;
 
   if (threadIdx.x == 0) {
@@ -1213,6 +1203,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = M.tmem_base;
+  // This grid may be a programmatic dependent of the scheduler (or of the
+  // previous decode): everything above touched only on-chip state; from
+  // here on the prerequisite grid has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const dsv4b_sched_meta sm = sched[blockIdx.x];
 
   if (warp < kProducerWarps) {
     if constexpr (is_bf16_layout(L)) {
@@ -1312,6 +1307,18 @@ int clusters_resident(int c) {
   return cache[dev][k] - 1;
 }
 
+// Whether the decode launch is a programmatic dependent: always on stream
+// launches; inside CUDA-graph capture only with DSV4B_PDL_IN_GRAPH=1.
+bool pdl_allowed(cudaStream_t stream) {
+  static const bool in_graph = [] {
+    const char* e = getenv("DSV4B_PDL_IN_GRAPH");
+    return e && e[0] == '1';
+  }();
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return false;
+  return cap == cudaStreamCaptureStatusNone || in_graph;
+}
+
 // 4-D TMA map of q, dims (innermost first) {d_qk, h_q, s_q, b}, box
 // {64, 64, 1, 1} with SWIZZLE_128B: one box = one Q^T chunk slot.  A size-1
 // dimension gets a nominal stride (its coordinate is always 0).
@@ -1348,13 +1355,25 @@ cudaError_t launch_decode_impl(const dsv4b_decode_params& p, const dsv4b_sched_m
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = SmemPlan<L>::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = c > 1 ? c : 1;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = c > 1 ? 1 : 0;
+  // Programmatic dependent launch: the CTAs set up while the previous grid
+  // (typically the scheduler of get_mla_metadata) drains, and wait for it
+  // in-kernel (griddepcontrol.wait) before reading anything it wrote.
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (pdl_allowed(stream)) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (c > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = c;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, sparse_decode_kernel<L>, p, sched, num_splits, lse_accum, o_accum, err,
                             c > 1 ? c : 1, q_map);
 }
