@@ -458,14 +458,23 @@ mqa_logits_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant
           float v[64];
           tmem_ld64(tmem + lane_base + acc * N, v);
           tc_wait_ld();
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          // Accumulators (s0, s1) and (s2, s3) as packed f32x2 pairs: one
+          // fma.rn.f32x2 per two heads (each lane an ordinary fp32 FMA, so
+          // the sums are bit-identical to four scalar accumulators).
+          uint64_t s01 = 0, s23 = 0;
 #pragma unroll
           for (int e = 0; e < 64; e += 4) {
-            s0 = fmaf(fmaxf(v[e], 0.f), wr[e], s0);
-            s1 = fmaf(fmaxf(v[e + 1], 0.f), wr[e + 1], s1);
-            s2 = fmaf(fmaxf(v[e + 2], 0.f), wr[e + 2], s2);
-            s3 = fmaf(fmaxf(v[e + 3], 0.f), wr[e + 3], s3);
+            uint64_t x01, x23, w01, w23;
+            asm("mov.b64 %0, {%1, %2};" : "=l"(x01) : "f"(fmaxf(v[e], 0.f)), "f"(fmaxf(v[e + 1], 0.f)));
+            asm("mov.b64 %0, {%1, %2};" : "=l"(x23) : "f"(fmaxf(v[e + 2], 0.f)), "f"(fmaxf(v[e + 3], 0.f)));
+            asm("mov.b64 %0, {%1, %2};" : "=l"(w01) : "f"(wr[e]), "f"(wr[e + 1]));
+            asm("mov.b64 %0, {%1, %2};" : "=l"(w23) : "f"(wr[e + 2]), "f"(wr[e + 3]));
+            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s01) : "l"(x01), "l"(w01));
+            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s23) : "l"(x23), "l"(w23));
           }
+          float s0, s1, s2, s3;
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(s0), "=f"(s1) : "l"(s01));
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(s2), "=f"(s3) : "l"(s23));
           res[0] = ((s0 + s1) + (s2 + s3)) * scale;
           done_sum = true;
         }
