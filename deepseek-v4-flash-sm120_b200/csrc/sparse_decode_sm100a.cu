@@ -126,7 +126,6 @@ struct Misc {
   uint64_t drain;  // end of the MMA issuer's tcgen05 work (abort path)
   uint32_t tmem_base;
   int abort;
-  uint32_t sink_word;  // target of the producers' load-completion fold
   uint32_t cl_live;    // cluster epilogue: bit i = cluster rank i holds a partial
   int q_loads;         // Q^T loads issued (thread 0); the abort path waits for the last
   alignas(16) float red[4][64];
@@ -199,22 +198,23 @@ __device__ __forceinline__ void load_q_tma(const CUtensorMap* q_map, uint32_t q_
 // columns = two 64-column SW128 chunk slots = one V32 scale tile = the slot
 // pair one PV M-block releases.
 //
-// Loads are split in two register phases per tile.  Phase A (pairs 0-1 and
-// the scales) is issued at the end of the previous tile together with an
-// L2 bulk prefetch of each whole row, and landed there.  Phase B (pairs 2-3
-// and MODEL1 RoPE) is issued after pairs 0-1 are stored and hits L2; the
-// V32 RoPE chunk is loaded after pair 3, while waiting for the previous PV.  A proxy fence
-// followed by an mbarrier arrive waits for all of the thread's outstanding
-// loads, so every hand-off happens with no load in flight.
+// Loads are pipelined pair by pair: right after a thread has stored chunk
+// pair m of tile t, it issues the loads of pair m of tile t+1 into the same
+// registers, so every load has about a whole tile period to land and the
+// load-store path sees a steady trickle instead of one burst per tile.  An
+// mbarrier arrive does not wait for the thread's loads in flight (measured
+// on B200: a release arrive with 24 loads outstanding takes ~100 cycles),
+// so the hand-offs are not delayed by them.  The scales of tile t+1 are
+// loaded once pair 3 of tile t (their last user) is stored, the V32 RoPE
+// chunk once its slot has been filled, and the indices of tile t+2 last.
 constexpr int kRowsPerThread = 4;
 
 template <int L>
 struct ProdRegs {
   RowSrc rs[kRowsPerThread];
-  uint4 fa[2][kRowsPerThread];  // phase A: pairs 0, 1
-  uint4 sc[kRowsPerThread];     // V32: 4 fp32 scales; MODEL1: 8 UE8M0 bytes in .x/.y
-  uint4 fb[2][kRowsPerThread];  // phase B: pairs 2, 3 (MODEL1 pair 3: fp8 or RoPE part 0)
-  uint4 rp[kRowsPerThread];     // V32 RoPE; MODEL1 RoPE part 1
+  uint4 f[4][kRowsPerThread];  // chunk pairs 0-3 (MODEL1 pair 3: fp8 or RoPE part 0)
+  uint4 sc[kRowsPerThread];    // V32: 4 fp32 scales; MODEL1: 8 UE8M0 bytes in .x/.y
+  uint4 rp[kRowsPerThread];    // V32 RoPE; MODEL1 RoPE part 1
 };
 
 // Flat cache index of tile row r, or -1 for padding (>= the row's attended
@@ -238,48 +238,33 @@ __device__ __forceinline__ void rows_of(const dsv4b_decode_params& p, const Tile
     R.rs[k] = row_src<L>(ts.kv, ts.page, ts.stride_block, ts.stride_row, ts.num_tokens, idx[k], true);
 }
 
+// Lane q's 16 bytes of chunk pair m of each of its rows (MODEL1 pair 3,
+// lanes 4-7: the 64 bf16 RoPE columns, 32 bytes per lane).
 template <int L>
-__device__ __forceinline__ void load_phase_a(int q, ProdRegs<L>& R) {
+__device__ __forceinline__ void load_pair(int m, int q, ProdRegs<L>& R) {
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) {
     const RowSrc& r = R.rs[k];
-    R.fa[0][k] = ldg_or_zero(r.valid, r.rec + 16 * q);
-    R.fa[1][k] = ldg_or_zero(r.valid, r.rec + 128 + 16 * q);
-    R.sc[k] = load_scales<L>(r);
-  }
-}
-
-template <int L>
-__device__ __forceinline__ void load_phase_b(int q, ProdRegs<L>& R) {
-#pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k) {
-    const RowSrc& r = R.rs[k];
-    R.fb[0][k] = ldg_or_zero(r.valid, r.rec + 256 + 16 * q);
-    if constexpr (L == DSV4B_LAYOUT_V32) {
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
-    } else if (q < 4) {  // MODEL1 pair 3: fp8 columns 384..447 ...
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + 384 + 16 * q);
-    } else {             // ... and the 64 bf16 RoPE columns
-      R.fb[1][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
+    if (L == DSV4B_LAYOUT_MODEL1 && m == 3 && q >= 4) {
+      R.f[3][k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4));
       R.rp[k] = ldg_or_zero(r.valid, r.rec + LayoutT<L>::kRopeOffset + 32 * (q - 4) + 16);
+    } else {
+      R.f[m][k] = ldg_or_zero(r.valid, r.rec + 128 * m + 16 * q);
     }
   }
 }
 
-// Folds registers into one word stored to shared memory: pins the loads
-// (and their completion) to this point, so the code generator cannot sink
-// them into the chunk loop where the latency would be exposed per chunk.
 template <int L>
-__device__ __forceinline__ void land_phase_a(const ProdRegs<L>& R, const int (&idx)[kRowsPerThread],
-                                             Misc& M) {
-  uint32_t x = 0;
+__device__ __forceinline__ void load_scales_all(ProdRegs<L>& R) {
 #pragma unroll
-  for (int k = 0; k < kRowsPerThread; ++k) {
-    x ^= R.fa[0][k].x ^ R.fa[0][k].y ^ R.fa[0][k].z ^ R.fa[0][k].w;
-    x ^= R.fa[1][k].x ^ R.fa[1][k].y ^ R.fa[1][k].z ^ R.fa[1][k].w;
-    x ^= R.sc[k].x ^ R.sc[k].y ^ R.sc[k].z ^ R.sc[k].w ^ (uint32_t)idx[k];
-  }
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(&M.sink_word)), "r"(x) : "memory");
+  for (int k = 0; k < kRowsPerThread; ++k) R.sc[k] = load_scales<L>(R.rs[k]);
+}
+
+template <int L>
+__device__ __forceinline__ void load_rope_v32(int q, ProdRegs<L>& R) {
+#pragma unroll
+  for (int k = 0; k < kRowsPerThread; ++k)
+    R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
 }
 
 // Scale of the 16 columns lane q holds in chunk pair m.
@@ -334,11 +319,12 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
   rows_of<L>(p, cur, idx, R);
-  load_phase_a<L>(q, R);
-  load_phase_b<L>(q, R);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) load_pair<L>(m, q, R);
+  load_scales_all<L>(R);
+  if constexpr (LT::kPInRopeSlot) load_rope_v32<L>(q, R);
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nxt.valid ? producer_index(p, nxt, row0 + 4 * k) : -1;
-  land_phase_a<L>(R, idx, M);
 
   int tile_count = 0, seg_count = 0;
   volatile int* abort_flag = &M.abort;
@@ -354,32 +340,13 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
     }
     if (ptid == 0) DSV4B_TR_ROLE(0, 1, tile_count);
     const uint32_t wait_par = (tile_count - 1) & 1;
+    const bool more = nxt.valid;
+    // This tile's loads are all issued: the row addresses of the next tile
+    // (its indices were loaded during the previous tile) take their place.
+    if (more) rows_of<L>(p, nxt, idx, R);
 
-    // pairs 0, 1 (phase A registers)
 #pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      DSV4B_TR_WARP(55, m);
-      if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
-      DSV4B_TR_WARP(51, m);
-#pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k)
-        store_pair_fp8(slot_s, m, row0 + 4 * k, q, R.fa[m][k], pair_scale<L>(R.sc[k], m, q));
-      DSV4B_TR_WARP(56, m);
-      fence_proxy_async_smem();
-      mbar_arrive(&M.full[2 * m]);
-      mbar_arrive(&M.full[2 * m + 1]);
-      DSV4B_TR_WARP(52, m);
-      if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
-    }
-    if constexpr (LayoutT<L>::kPInRopeSlot) {
-      // V32 RoPE chunk: issued here so it lands while pairs 2, 3 are stored.
-#pragma unroll
-      for (int k = 0; k < kRowsPerThread; ++k)
-        R.rp[k] = ldg_or_zero(R.rs[k].valid, R.rs[k].rec + LayoutT<L>::kRopeOffset + 16 * q);
-    }
-    // pairs 2, 3 (phase B registers)
-#pragma unroll
-    for (int m = 2; m < 4; ++m) {
+    for (int m = 0; m < 4; ++m) {
       DSV4B_TR_WARP(55, m);
       if (tile_count > 0 && !mbar_wait(&M.empty[m], wait_par, abort_flag, err)) return;
       DSV4B_TR_WARP(51, m);
@@ -388,10 +355,10 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
         const int row = row0 + 4 * k;
         if (L == DSV4B_LAYOUT_MODEL1 && m == 3 && q >= 4) {
           const uint32_t slot = slot_s + 7 * kSlotBytes;  // MODEL1 RoPE chunk
-          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.fb[1][k]);
+          sts_v4(slot + sw128_off(row, 2 * (q - 4)), R.f[3][k]);
           sts_v4(slot + sw128_off(row, 2 * (q - 4) + 1), R.rp[k]);
         } else {
-          store_pair_fp8(slot_s, m, row, q, R.fb[m - 2][k], pair_scale<L>(R.sc[k], m, q));
+          store_pair_fp8(slot_s, m, row, q, R.f[m][k], pair_scale<L>(R.sc[k], m, q));
         }
       }
       DSV4B_TR_WARP(56, m);
@@ -400,8 +367,9 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
       mbar_arrive(&M.full[2 * m + 1]);
       DSV4B_TR_WARP(52, m);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, 2 * m + 1);
+      if (more) load_pair<L>(m, q, R);
     }
-    if constexpr (LayoutT<L>::kPInRopeSlot) {
+    if constexpr (LT::kPInRopeSlot) {
       // V32 RoPE chunk (slot NCH-1, shared with P^T): after the previous PV.
       DSV4B_TR_WARP(55, 4);
       if (tile_count > 0 && !mbar_wait(&M.empty[4], wait_par, abort_flag, err)) return;
@@ -414,20 +382,13 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
       mbar_arrive(&M.full[NCH - 1]);
       DSV4B_TR_WARP(52, 4);
       if (ptid == 0) DSV4B_TR_ROLE(0, 2, NCH - 1);
+      if (more) load_rope_v32<L>(q, R);
     }
-
-    // The next tile's loads, then the indices of the tile after it.
     const TileCursor nn = cursor_next(p, sm, nxt);
-    if (nxt.valid) {
-      DSV4B_TR_WARP(57, tile_count);
-      rows_of<L>(p, nxt, idx, R);
-      load_phase_a<L>(q, R);
-      load_phase_b<L>(q, R);
-      DSV4B_TR_WARP(50, tile_count);
+    if (more) {
+      load_scales_all<L>(R);
 #pragma unroll
       for (int k = 0; k < kRowsPerThread; ++k) idx[k] = nn.valid ? producer_index(p, nn, row0 + 4 * k) : -1;
-      land_phase_a<L>(R, idx, M);
-      DSV4B_TR_WARP(58, tile_count);
     }
     if (ptid == 0) DSV4B_TR_ROLE(0, 6, tile_count);
 
