@@ -316,9 +316,11 @@ __device__ void run_producer(const dsv4b_decode_params& p, const dsv4b_sched_met
 
   ProdRegs<L> R;
   int idx[kRowsPerThread];
+  if (ptid == 0) DSV4B_TR_ROLE(0, 42, cur.t);
 #pragma unroll
   for (int k = 0; k < kRowsPerThread; ++k) idx[k] = producer_index(p, cur, row0 + 4 * k);
   rows_of<L>(p, cur, idx, R);
+  if (ptid == 0) DSV4B_TR_ROLE(0, 43, idx[0] & 0xFFFF);
 #pragma unroll
   for (int m = 0; m < 4; ++m) load_pair<L>(m, q, R);
   load_scales_all<L>(R);
@@ -1151,6 +1153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
       s_trace_base[127] = gt;  // role 0 last slot: globaltimer at start
       s_trace_base[126] = (unsigned long long)clock64();
+      DSV4B_TR_ROLE(0, 44, 0);
     }
 #endif
     fence_mbarrier_init();
@@ -1167,8 +1170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // This grid may be a programmatic dependent of the scheduler (or of the
   // previous decode): everything above touched only on-chip state; from
   // here on the prerequisite grid has completed and its writes are visible.
+  if (threadIdx.x == 0) DSV4B_TR_ROLE(0, 40, 0);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const dsv4b_sched_meta sm = sched[blockIdx.x];
+  if (threadIdx.x == 0) DSV4B_TR_ROLE(0, 41, sm.begin_req_idx);
 
   if (warp < kProducerWarps) {
     if constexpr (is_bf16_layout(L)) {
