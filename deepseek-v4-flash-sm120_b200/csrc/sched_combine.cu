@@ -244,21 +244,31 @@ __global__ void __launch_bounds__(kSchedThreads)
 // One 128-thread CTA per (query row, head); thread t owns dims 4t..4t+3.
 // The decode kernel leaves split partials o_accum[split][h_q][512] (already
 // divided by the split's own row sum) and lse_accum[split][h_q].
-constexpr int kCombineThreads = kDv / 4;  // 128
-constexpr int kCombineRegSplits = 16;       // splits held in registers; more loop
+constexpr int kCombineThreads = kDv / 4;  // 128 per head
+// Two shapes, chosen per launch by the number of query rows (with 148
+// scheduler parts, few rows mean many splits per row):
+//  * few rows: one head per CTA, up to 16 splits held in registers
+//    (127 registers, every split's load in flight at once);
+//  * 16 rows or more (<= ~10 splits per row): four heads per CTA and 8
+//    splits in registers (64 registers, twice the resident warps), which
+//    measured 376 vs 390 us at config 4 and 35.8 vs 37.9 us at 16 rows, but
+//    2-4 us slower at 1-8 rows.
+constexpr int kCombineRowsForWide = 16;
 
 // Launched (outside CUDA-graph capture) as a programmatic dependent of the
 // decode kernel: the CTAs start while the decode grid drains and wait here
 // for its completion (and the visibility of its partials) instead of paying
 // a full launch gap.
-__global__ void __launch_bounds__(kCombineThreads)
+template <int kCombineHeads, int kCombineRegSplits>
+__global__ void __launch_bounds__(kCombineThreads * kCombineHeads)
     combine_kernel(const dsv4b_decode_params p, const int32_t* __restrict__ num_splits,
                    const float* __restrict__ lse_accum, const float* __restrict__ o_accum) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int r = blockIdx.x, head = blockIdx.y, t = threadIdx.x;
+  const int r = blockIdx.x, t = threadIdx.x % kCombineThreads;
+  const int head = blockIdx.y * kCombineHeads + threadIdx.x / kCombineThreads;
   const int s0 = __ldg(num_splits + r), s1 = __ldg(num_splits + r + 1);
   const int n = s1 - s0;
-  if (n <= 1) return;  // written by the decode kernel
+  if (n <= 1 || head >= p.h_q) return;  // n <= 1: written by the decode kernel
   constexpr float kLog2e = 1.4426950408889634f;
   const float* lse_col = lse_accum + (int64_t)s0 * p.h_q + head;
   const float4* src = reinterpret_cast<const float4*>(o_accum + ((int64_t)s0 * p.h_q + head) * kDv) + t;
@@ -381,8 +391,10 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
 cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_splits,
                            const float* lse_accum, const float* o_accum, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.b * p.s_q, p.h_q, 1);
-  cfg.blockDim = dim3(kCombineThreads, 1, 1);
+  const bool wide = p.b * p.s_q >= kCombineRowsForWide;
+  const int heads = wide ? 4 : 1;
+  cfg.gridDim = dim3(p.b * p.s_q, (p.h_q + heads - 1) / heads, 1);
+  cfg.blockDim = dim3(kCombineThreads * heads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   // Stream launches: a programmatic dependent of the decode kernel, so its
@@ -397,7 +409,8 @@ cudaError_t launch_combine(const dsv4b_decode_params& p, const int32_t* num_spli
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = cap == cudaStreamCaptureStatusNone ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, combine_kernel, p, num_splits, lse_accum, o_accum);
+  return wide ? cudaLaunchKernelEx(&cfg, combine_kernel<4, 8>, p, num_splits, lse_accum, o_accum)
+              : cudaLaunchKernelEx(&cfg, combine_kernel<1, 16>, p, num_splits, lse_accum, o_accum);
 }
 
 cudaError_t launch_gather_dequant(int layout, const void* kv, int num_blocks, int page_block_size,
