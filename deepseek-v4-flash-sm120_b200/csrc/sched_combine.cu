@@ -29,10 +29,14 @@ namespace dsv4b {
 
 namespace {
 
+// One CTA; 1024 threads, or a single warp when there are at most 32 query
+// rows (every scan is then a shuffle scan with no block barrier, which is
+// what a small batch's graph-captured step waits on).
 constexpr int kSchedThreads = 1024;
 
-// Exclusive block-wide scan of v over kSchedThreads threads; returns the
-// prefix for this thread and writes the block total to *total.
+// Exclusive scan of v over the NT threads of the block; returns the prefix
+// for this thread and writes the block total to *total.
+template <int NT>
 __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -41,10 +45,14 @@ __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
     const int y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
+  if constexpr (NT == 32) {
+    *total = __shfl_sync(0xffffffffu, x, 31);
+    return x - v;
+  }
   if (lane == 31) scratch[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = scratch[lane];
+    int w = lane < NT / 32 ? scratch[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, w, o);
@@ -76,7 +84,8 @@ __device__ __forceinline__ dsv4b_sched_meta empty_record() {
   return m;
 }
 
-__global__ void __launch_bounds__(kSchedThreads)
+template <int NT>
+__global__ void __launch_bounds__(NT)
     sched_meta_kernel(const dsv4b_decode_params p, int num_sm_parts, int cluster_c,
                       dsv4b_sched_meta* sched, int32_t* num_splits) {
   // scratch first: its base stays 16-byte aligned whatever R is, so the
@@ -92,11 +101,11 @@ __global__ void __launch_bounds__(kSchedThreads)
 
   // 1. tiles per query row -> exclusive prefix
   int carry = 0;
-  for (int base = 0; base < R; base += kSchedThreads) {
+  for (int base = 0; base < R; base += NT) {
     const int r = base + threadIdx.x;
     const int n = r < R ? req_info(p, r).nt : 0;
     int tot;
-    const int ex = block_exclusive_scan(n, scratch, &tot);
+    const int ex = block_exclusive_scan<NT>(n, scratch, &tot);
     if (r < R) tile_off[r] = carry + ex;
     carry += tot;
   }
@@ -109,8 +118,8 @@ __global__ void __launch_bounds__(kSchedThreads)
     // Cluster plan: row r owns parts r*C .. r*C+C-1 (one cluster), its
     // tiles shared evenly; the cluster merges the row itself, so every row
     // counts as one split for the combine kernel.
-    for (int r = threadIdx.x; r <= R; r += kSchedThreads) num_splits[r] = r;
-    for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+    for (int r = threadIdx.x; r <= R; r += NT) num_splits[r] = r;
+    for (int part = threadIdx.x; part < num_sm_parts; part += NT) {
       dsv4b_sched_meta m = empty_record();
       const int r = part / cluster_c, j = part - r * cluster_c;
       if (r < R) {
@@ -136,39 +145,39 @@ __global__ void __launch_bounds__(kSchedThreads)
     // upper end always fits since R <= parts); every step is uniform
     // across the block.
     int max_t = 0;
-    for (int r = threadIdx.x; r < R; r += kSchedThreads) max_t = max(max_t, tile_off[r + 1] - tile_off[r]);
+    for (int r = threadIdx.x; r < R; r += NT) max_t = max(max_t, tile_off[r + 1] - tile_off[r]);
     for (int o = 16; o > 0; o >>= 1) max_t = max(max_t, __shfl_xor_sync(0xffffffffu, max_t, o));
     if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = max_t;
     __syncthreads();
     int hi = 0;
-    for (int w = 0; w < kSchedThreads / 32; ++w) hi = max(hi, scratch[w]);
+    for (int w = 0; w < NT / 32; ++w) hi = max(hi, scratch[w]);
     int lo = 1;
     __syncthreads();
     while (lo < hi) {
       const int mid = (lo + hi) / 2;
       int tot_parts = 0;
-      for (int base = 0; base < R; base += kSchedThreads) {
+      for (int base = 0; base < R; base += NT) {
         const int r = base + threadIdx.x;
         const int n = r < R ? (tile_off[r + 1] - tile_off[r] + mid - 1) / mid : 0;
         int tot;
-        block_exclusive_scan(n, scratch, &tot);
+        block_exclusive_scan<NT>(n, scratch, &tot);
         tot_parts += tot;
       }
       if (tot_parts <= num_sm_parts) hi = mid; else lo = mid + 1;
     }
     const int tcap = lo;
     carry = 0;
-    for (int base = 0; base < R; base += kSchedThreads) {
+    for (int base = 0; base < R; base += NT) {
       const int r = base + threadIdx.x;
       const int k = r < R ? (tile_off[r + 1] - tile_off[r] + tcap - 1) / tcap : 0;
       int tot;
-      const int ex = block_exclusive_scan(k, scratch, &tot);
+      const int ex = block_exclusive_scan<NT>(k, scratch, &tot);
       if (r < R) part_off[r] = num_splits[r] = carry + ex;
       carry += tot;
     }
     if (threadIdx.x == 0) part_off[R] = num_splits[R] = carry;
     __syncthreads();
-    for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+    for (int part = threadIdx.x; part < num_sm_parts; part += NT) {
       dsv4b_sched_meta m = empty_record();
       if (part < part_off[R]) {
         int a = 0, z = R - 1;  // the row r with part_off[r] <= part < part_off[r + 1]
@@ -193,7 +202,7 @@ __global__ void __launch_bounds__(kSchedThreads)
 
   // 2. splits per row -> exclusive prefix = num_splits
   carry = 0;
-  for (int base = 0; base < R; base += kSchedThreads) {
+  for (int base = 0; base < R; base += NT) {
     const int r = base + threadIdx.x;
     int n = 0;
     if (r < R) {
@@ -202,7 +211,7 @@ __global__ void __launch_bounds__(kSchedThreads)
       n = last - first + 1;
     }
     int tot;
-    const int ex = block_exclusive_scan(n, scratch, &tot);
+    const int ex = block_exclusive_scan<NT>(n, scratch, &tot);
     if (r < R) num_splits[r] = carry + ex;
     carry += tot;
   }
@@ -212,7 +221,7 @@ __global__ void __launch_bounds__(kSchedThreads)
   __syncthreads();
 
   // 3. one record per part
-  for (int part = threadIdx.x; part < num_sm_parts; part += kSchedThreads) {
+  for (int part = threadIdx.x; part < num_sm_parts; part += NT) {
     dsv4b_sched_meta m = empty_record();
     if (part < P_eff) {
       const long long t0 = (long long)part * T / P_eff;
@@ -378,13 +387,16 @@ cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    e = cudaFuncSetAttribute(sched_meta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(sched_meta_kernel<kSchedThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((32 + 2 * (kMaxSchedRows + 1)) * sizeof(int)));
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  sched_meta_kernel<<<1, kSchedThreads, smem, stream>>>(p, num_sm_parts, plan_cluster_size(p, num_sm_parts),
-                                                        sched, num_splits);
+  const int cc = plan_cluster_size(p, num_sm_parts);
+  if (R <= 32)
+    sched_meta_kernel<32><<<1, 32, smem, stream>>>(p, num_sm_parts, cc, sched, num_splits);
+  else
+    sched_meta_kernel<kSchedThreads><<<1, kSchedThreads, smem, stream>>>(p, num_sm_parts, cc, sched, num_splits);
   return cudaGetLastError();
 }
 
