@@ -1274,11 +1274,13 @@ int clusters_resident(int c) {
 }
 
 // Whether the decode launch is a programmatic dependent: always on stream
-// launches; inside CUDA-graph capture only with DSV4B_PDL_IN_GRAPH=1.
+// launches, and inside CUDA-graph capture too unless DSV4B_PDL_IN_GRAPH=0
+// (with the scheduler captured before it, a graphed b 1-32 step measured
+// ~2 us faster with the programmatic edge; without it, the same).
 bool pdl_allowed(cudaStream_t stream) {
   static const bool in_graph = [] {
     const char* e = getenv("DSV4B_PDL_IN_GRAPH");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return false;
