@@ -80,9 +80,11 @@ def parse():
     ap.add_argument("--no-next-rows", action="store_true",
                     help="skip the writer / indexer summaries in the config-1 line")
     ap.add_argument("--json-out", default=None)
-    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits", "prefill"], default="decode",
+    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits", "prefill", "mma_rates"],
+                    default="decode",
                     help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
-                         "logits (fp8_paged_mqa_logits) over config 1's contexts")
+                         "logits (fp8_paged_mqa_logits) over config 1's contexts; mma_rates: cycles per "
+                         "tcgen05.mma of the decode kernel's operand shapes (resident operands)")
     ap.add_argument("--next-n", type=int, default=1, help="mqa_logits: query rows per request")
     ap.add_argument("--page-order", choices=["random", "sequential"], default="random",
                     help="mqa_logits: physical order of each request's pages (block table)")
@@ -885,6 +887,52 @@ def run_mqa_logits(args):
     return line
 
 
+def run_mma_rates(args):
+    """Cycles per tcgen05.mma (kind::f16, M 128, K 16) for the decode
+    kernel's operand shapes with resident shared-memory operands
+    (dsv4b_mma_rate_probe): one CTA alone and one CTA per SM at once; the
+    median over CTAs of each CTA's best of six chains.  The dense bf16 peak
+    per SM per cycle (measured TFLOP/s / 148 SMs / the sampled clock) is the
+    denominator of "frac"."""
+    import torch
+
+    from deepseek_v4_kernel import _lib
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    lib = _lib.lib
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    _, bf16_tflops, peak_src = measured_peaks()
+    clocks = ClockSampler(0)
+    clocks.start()
+    shapes = {0: ("qk_n64_kmajor", 64), 1: ("pv_n64_mnmajor", 64), 2: ("qk_a_n128", 128), 3: ("qk_a_n256", 256),
+              4: ("qk_n64_kmajor_predesc", 64), 5: ("pv_n64_mnmajor_predesc", 64)}
+    out = torch.zeros(2 * sms, dtype=torch.int64, device=device)
+    rows = []
+    for shape, (name, n) in shapes.items():
+        for ctas in (1, sms):
+            rc = lib.dsv4b_mma_rate_probe(shape, ctas, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise RuntimeError(_lib.STATUS.get(rc, rc))
+            torch.cuda.synchronize()
+            v = out[: 2 * ctas].view(ctas, 2).cpu()
+            if (v[:, 0] < 0).any():
+                raise RuntimeError("mma probe: a bounded wait gave up")
+            cyc = float(v[:, 0].double().median())
+            mmas = int(v[0, 1])
+            rows.append({"shape": name, "n": n, "ctas": ctas, "mmas": mmas, "cycles": cyc,
+                         "cycles_per_mma": round(cyc / mmas, 1), "flop_per_cycle": round(2 * 128 * n * 16 * mmas / cyc)})
+    clk = clocks.stop()
+    # cycles do not depend on the clock; the measured cuBLAS peak is turned
+    # into flop per SM cycle at the GPU's maximum SM clock
+    mhz = clk.get("sm_max_mhz") or 1965.0
+    peak_per_cycle = bf16_tflops * 1e12 / sms / (mhz * 1e6)
+    for r in rows:
+        r["frac_of_measured_peak"] = round(r["flop_per_cycle"] / peak_per_cycle, 3)
+    return {"metric": "tcgen05_mma_cycles", "unit": "SM cycles per MMA", "op": "mma_rates",
+            "peak_flop_per_cycle_per_sm": round(peak_per_cycle), "peak_source": peak_src,
+            "peak_clock_mhz": mhz, "clocks": clk, "rates": rows}
+
+
 def run_prefill(args):
     """One step = one flash_mla_sparse_fwd call (sparse prefill, bf16 KV):
     s_q 4096 query tokens x h_q 128 heads, d_qk 512, top-k 2048 over a
@@ -1060,9 +1108,10 @@ def run_sweep(args):
 
 def main():
     args = parse()
-    if args.op in ("kv_write", "mqa_logits", "prefill"):
+    if args.op in ("kv_write", "mqa_logits", "prefill", "mma_rates"):
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
-            line = {"kv_write": run_kv_write, "mqa_logits": run_mqa_logits, "prefill": run_prefill}[args.op](args)
+            line = {"kv_write": run_kv_write, "mqa_logits": run_mqa_logits, "prefill": run_prefill,
+                    "mma_rates": run_mma_rates}[args.op](args)
             print(json.dumps(line), flush=True)
             if args.json_out:
                 with open(args.json_out, "w") as f:

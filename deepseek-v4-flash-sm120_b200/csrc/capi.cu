@@ -281,6 +281,14 @@ int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks, int page_bl
                                               static_cast<cudaStream_t>(stream)));
 }
 
+int dsv4b_mma_rate_probe(int shape, int ctas, long long* out, void* stream) {
+  if (shape < 0 || shape > 5 || ctas <= 0 || ctas > 65535 || !out || !aligned(out, 16))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
+  if (rc) return rc;
+  return cuda_rc(dsv4b::launch_mma_probe(shape, ctas, out, static_cast<cudaStream_t>(stream)));
+}
+
 int dsv4b_kv_cache_write(int layout, const void* nope, int64_t stride_nope, const void* rope,
                          int64_t stride_rope, const void* slot_mapping, int slot_bytes, int64_t n,
                          void* kv, int num_blocks, int page_block_size, int64_t stride_kv_block,

@@ -42,6 +42,12 @@ cudaError_t set_decode_test_stall(int stall);
 // launch and the C ABI all decide with this one function.
 int plan_cluster_size(const dsv4b_decode_params& p, int num_sm_parts);
 
+// Measurement: per CTA, the best-of-six cycles of one decode MMA shape's
+// chain and its MMA count (out[2 i], out[2 i + 1]; cycles -1 after a wait
+// gave up).  Shapes: 0 QK^T, 1 PV, 2 QK^T A with N 128, 3 with N 256,
+// 4 and 5: 0 and 1 from precomputed descriptors.
+cudaError_t launch_mma_probe(int shape, int ctas, long long* out, cudaStream_t stream);
+
 cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
                               dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream);
 

@@ -188,6 +188,17 @@ DSV4B_API int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks,
                          int64_t stride_kv_row, const int32_t* indices, int n,
                          void* out_bf16, void* stream);
 
+/* Measurement: time the decode kernel's tcgen05.mma shapes with resident
+ * shared-memory operands, one chain per CTA on `ctas` CTAs.  out (device,
+ * 16-byte aligned, 2 * ctas int64): per CTA the best of six repetitions in
+ * SM cycles (-1 if its bounded wait gave up) and the number of MMAs in the
+ * chain.  shape 0: QK^T (M 128, N 64, A and B K-major, 36 MMAs); 1: PV
+ * (M 128, N 64, A and B MN-major, 32 MMAs); 2: the QK^T A operand with
+ * N 128 (16 MMAs); 3: with N 256 (8 MMAs); 4, 5: shapes 0, 1 issued from
+ * precomputed descriptors.  No reference counterpart: it
+ * backs the tensor-core figures of the decode roofline. */
+DSV4B_API int dsv4b_mma_rate_probe(int shape, int ctas, long long* out, void* stream);
+
 /* KV-cache writer: quantise n bf16 tokens into the cache's FP8 format and
  * scatter them to their slots (flat page * page_block_size + offset).
  *   layout V32:    nope = latent [n, 512], rope = [n, 64]; 656-B records

@@ -437,3 +437,22 @@ def test_extra_kv_sidecar_cluster_plan():
     ref_out, ref_lse = oracle_for(bt.q, bt.kv, bt.indices, None, bt.attn_sink, bt.sm_scale, "v32",
                                   extra=extra)
     assert_matches(out, lse, ref_out, ref_lse)
+
+
+@pytest.mark.gpu
+def test_mma_rate_probe_reports_every_shape():
+    """dsv4b_mma_rate_probe (the measurement behind the decode kernel's
+    tensor-core roofline) runs each shape's chain and reports its MMA
+    count and a positive cycle count per CTA."""
+    import torch
+    from deepseek_v4_kernel import _lib
+    torch.cuda.set_device(0)
+    out = torch.zeros(2 * 4, dtype=torch.int64, device="cuda")
+    for shape, mmas in ((0, 36), (1, 32), (2, 16), (3, 8), (4, 36), (5, 32)):
+        rc = _lib.lib.dsv4b_mma_rate_probe(shape, 4, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, _lib.STATUS.get(rc, rc)
+        torch.cuda.synchronize()
+        v = out.view(4, 2).cpu()
+        assert (v[:, 1] == mmas).all(), v
+        assert (v[:, 0] > 0).all(), v
+    assert _lib.lib.dsv4b_mma_rate_probe(6, 4, out.data_ptr(), None) == -1
