@@ -19,7 +19,8 @@
 //
 // K3 merges splits: lse = log sum_i exp(lse_i), O = sum_i exp(lse_i - lse)
 // O_i, then the sink epilogue of tests/reference.py:124-129.  One CTA per
-// (query row, head); rows with a single split were written by K1 directly.
+// (query row, head) or per (query row, four heads) by batch size; rows with
+// a single split were written by K1 directly.
 #include <cuda_bf16.h>
 
 #include "dsv4b_internal.cuh"
