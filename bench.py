@@ -80,11 +80,12 @@ def parse():
     ap.add_argument("--no-next-rows", action="store_true",
                     help="skip the writer / indexer summaries in the config-1 line")
     ap.add_argument("--json-out", default=None)
-    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits", "prefill", "mma_rates"],
+    ap.add_argument("--op", choices=["decode", "kv_write", "mqa_logits", "prefill", "mma_rates", "gather_rates"],
                     default="decode",
                     help="kv_write: the KV-cache writer (quantise + scatter); mqa_logits: the indexer "
                          "logits (fp8_paged_mqa_logits) over config 1's contexts; mma_rates: cycles per "
-                         "tcgen05.mma of the decode kernel's operand shapes (resident operands)")
+                         "tcgen05.mma of the decode kernel's operand shapes (resident operands); "
+                         "gather_rates: random whole-row gathers per load mechanism")
     ap.add_argument("--next-n", type=int, default=1, help="mqa_logits: query rows per request")
     ap.add_argument("--page-order", choices=["random", "sequential"], default="random",
                     help="mqa_logits: physical order of each request's pages (block table)")
@@ -887,6 +888,60 @@ def run_mqa_logits(args):
     return line
 
 
+def run_gather_rates(args):
+    """Random whole-row gathers (656-B V32 records, config 1's cache
+    geometry: 16,384 pages x 256 rows, 2.75 GB) into all 148 SMs with
+    nothing else running, per mechanism (dsv4b_gather_rate_probe: 16-byte
+    register loads, or one bulk copy per row): config 1's 65,536 rows per
+    launch and a 4x larger gather; L2 flushed before every launch, CUDA
+    events, median of --steps launches."""
+    import statistics as st
+
+    import torch
+
+    from deepseek_v4_kernel import _lib
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    lib = _lib.lib
+    row_bytes, nrows_cache = 656, 16384 * 256
+    kv = torch.empty(nrows_cache * row_bytes, dtype=torch.uint8, device=device)
+    scratch = torch.zeros(148 * 256 + 4, dtype=torch.int32, device=device)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    g = torch.Generator(device="cpu").manual_seed(7)
+    hbm, _, peak_src = measured_peaks()
+    stream = torch.cuda.current_stream()
+    out = []
+    clocks = ClockSampler(0)
+    clocks.start()
+    for n in (65536, 262144):
+        rows = torch.randint(0, nrows_cache, (n,), generator=g, dtype=torch.int32).to(device)
+        for mech, name in ((0, "register_16B_loads"), (1, "bulk_copy_per_row")):
+            ts = []
+            for it in range(args.warmup + args.steps):
+                flush.zero_()
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                rc = lib.dsv4b_gather_rate_probe(mech, kv.data_ptr(), row_bytes, row_bytes, rows.data_ptr(), n,
+                                                 scratch.data_ptr(), scratch.numel() * 4, stream.cuda_stream)
+                e.record()
+                if rc != 0:
+                    raise RuntimeError(_lib.STATUS.get(rc, rc))
+                torch.cuda.synchronize()
+                if it >= args.warmup:
+                    ts.append(a.elapsed_time(e) * 1e3)
+            if int(scratch[-4].item()) != 0:
+                raise RuntimeError("gather probe: a bounded wait gave up")
+            us = st.median(ts)
+            gbs = n * row_bytes / us / 1e3
+            out.append({"mechanism": name, "rows": n, "bytes": n * row_bytes, "us": round(us, 2),
+                        "GB_per_s": round(gbs, 1), "GB_per_s_per_sm": round(gbs / 148, 1),
+                        "frac_of_measured_hbm": round(gbs / hbm, 3)})
+    clk = clocks.stop()
+    return {"metric": "random_row_gather_GBps", "unit": "GB/s", "op": "gather_rates", "row_bytes": row_bytes,
+            "cache_bytes": nrows_cache * row_bytes, "hbm_peak_gbs": hbm, "peak_source": peak_src,
+            "l2": "flushed before every launch (256 MiB write)", "clocks": clk, "rates": out}
+
+
 def run_mma_rates(args):
     """Cycles per tcgen05.mma (kind::f16, M 128, K 16) for the decode
     kernel's operand shapes with resident shared-memory operands
@@ -1108,10 +1163,10 @@ def run_sweep(args):
 
 def main():
     args = parse()
-    if args.op in ("kv_write", "mqa_logits", "prefill", "mma_rates"):
+    if args.op in ("kv_write", "mqa_logits", "prefill", "mma_rates", "gather_rates"):
         if int(os.environ.get("RANK", "0")) == 0 and args.impl == "ours":
             line = {"kv_write": run_kv_write, "mqa_logits": run_mqa_logits, "prefill": run_prefill,
-                    "mma_rates": run_mma_rates}[args.op](args)
+                    "mma_rates": run_mma_rates, "gather_rates": run_gather_rates}[args.op](args)
             print(json.dumps(line), flush=True)
             if args.json_out:
                 with open(args.json_out, "w") as f:

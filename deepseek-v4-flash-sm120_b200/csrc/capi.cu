@@ -289,6 +289,20 @@ int dsv4b_mma_rate_probe(int shape, int ctas, long long* out, void* stream) {
   return cuda_rc(dsv4b::launch_mma_probe(shape, ctas, out, static_cast<cudaStream_t>(stream)));
 }
 
+int dsv4b_gather_rate_probe(int mechanism, const void* kv, int64_t row_stride, int row_bytes,
+                            const int32_t* rows, int n, void* scratch, size_t scratch_bytes, void* stream) {
+  if (mechanism < 0 || mechanism > 1 || !kv || !rows || n <= 0 || row_bytes <= 0 || row_bytes % 16 ||
+      row_bytes > 1536 || row_stride < row_bytes || row_stride % 16 || !aligned(kv, 16) || !scratch ||
+      scratch_bytes < (size_t)(148 * 256 + 4) * 4 || !aligned(scratch, 16))
+    return DSV4B_ERR_INVALID_ARGUMENT;
+  int rc = current_arch_ok();
+  if (rc) return rc;
+  uint32_t* sink = static_cast<uint32_t*>(scratch);
+  int* err = reinterpret_cast<int*>(sink + 148 * 256);
+  return cuda_rc(dsv4b::launch_gather_rate(mechanism, kv, row_stride, row_bytes, rows, n, sink, err,
+                                           static_cast<cudaStream_t>(stream)));
+}
+
 int dsv4b_kv_cache_write(int layout, const void* nope, int64_t stride_nope, const void* rope,
                          int64_t stride_rope, const void* slot_mapping, int slot_bytes, int64_t n,
                          void* kv, int num_blocks, int page_block_size, int64_t stride_kv_block,

@@ -48,6 +48,12 @@ int plan_cluster_size(const dsv4b_decode_params& p, int num_sm_parts);
 // 4 and 5: 0 and 1 from precomputed descriptors.
 cudaError_t launch_mma_probe(int shape, int ctas, long long* out, cudaStream_t stream);
 
+// Measurement: gather n random rows (row numbers in `rows`) of row_bytes
+// each with one mechanism (0 register loads, 1 per-row bulk copies) on 148
+// CTAs; sink takes 148 x 256 words, err the timeout status.
+cudaError_t launch_gather_rate(int mechanism, const void* kv, int64_t row_stride, int row_bytes,
+                               const int32_t* rows, int n, uint32_t* sink, int* err, cudaStream_t stream);
+
 cudaError_t launch_sched_meta(const dsv4b_decode_params& p, int num_sm_parts,
                               dsv4b_sched_meta* sched, int32_t* num_splits, cudaStream_t stream);
 

@@ -142,3 +142,122 @@ cudaError_t launch_mma_probe(int shape, int ctas, long long* out, cudaStream_t s
 }
 
 }  // namespace dsv4b
+
+// ------------------------------------------------------------- gather rate
+// Measurement kernel: how fast one mechanism gathers random whole cache
+// rows (the decode kernel's access pattern) into an SM, with nothing else
+// running.  Each CTA takes a contiguous share of the n row numbers.
+//  mechanism 0: 16-byte ld.global.nc by all 256 threads with the decode
+//               kernel's lane mapping (12 loads in flight per thread),
+//               folded into registers;
+//  mechanism 1: one cp.async.bulk per row into shared memory, issued by
+//               lane 0 of each of the 8 warps into its own 4-stage ring of
+//               4 rows, completing on mbarriers (bounded waits).
+// Rows are row_bytes long (a multiple of 16) at kv + row * row_stride.
+namespace dsv4b {
+namespace {
+
+constexpr int kGatherThreads = 256;
+constexpr int kGatherStages = 4, kGatherRowsPerStage = 4;
+
+__global__ void __launch_bounds__(kGatherThreads)
+    gather_rate_kernel(int mechanism, const uint8_t* __restrict__ kv, int64_t row_stride, int row_bytes,
+                       const int32_t* __restrict__ rows, int n, uint32_t* __restrict__ sink, int* err) {
+  extern __shared__ __align__(128) uint8_t gsm[];
+  const int per = (n + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * per, r1 = min(n, r0 + per);
+  if (r0 >= r1) return;
+  uint32_t x = 0;
+  if (mechanism == 0) {
+    // K1's mapping: a warp takes 4 rows per pass, lane q = lane & 7 reads
+    // the 16-byte pieces q, q + 8, ... of row lane >> 3 (a warp load covers
+    // 4 rows x 128 contiguous bytes); two passes (8 rows, up to 12 loads per
+    // thread) are in flight before any is used, their row numbers loaded
+    // one step ahead.
+    const int pieces = row_bytes / 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = lane & 7, sub = lane >> 3;
+    int ra = r0 + warp * 8 + sub, rb = ra + 4;
+    int ia = ra < r1 ? __ldg(rows + ra) : -1, ib = rb < r1 ? __ldg(rows + rb) : -1;
+    for (int base = r0 + warp * 8; base < r1; base += 8 * 8) {
+      const int nra = base + 64 + sub, nrb = nra + 4;
+      const int nia = nra < r1 ? __ldg(rows + nra) : -1, nib = nrb < r1 ? __ldg(rows + nrb) : -1;
+      uint4 v[12];
+#pragma unroll
+      for (int u = 0; u < 6; ++u) {
+        const int pc = q + 8 * u;
+        v[u] = (ia >= 0 && pc < pieces) ? ldg_nc_v4(kv + (int64_t)ia * row_stride + 16 * pc) : make_uint4(0, 0, 0, 0);
+        v[6 + u] = (ib >= 0 && pc < pieces) ? ldg_nc_v4(kv + (int64_t)ib * row_stride + 16 * pc) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 12; ++u) x ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
+      ia = nia;
+      ib = nib;
+    }
+  } else {
+    __shared__ uint64_t bars[8][kGatherStages];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0)
+      for (int s = 0; s < kGatherStages; ++s) mbar_init(&bars[warp][s], 1);
+    fence_mbarrier_init();
+    __syncwarp();
+    const uint32_t ring = smem_u32(gsm) + (uint32_t)warp * kGatherStages * kGatherRowsPerStage * row_bytes;
+    if (lane == 0) {
+      int j = 0;
+      bool ok = true;
+      for (int r = r0 + warp * kGatherRowsPerStage; r < r1 && ok; r += 8 * kGatherRowsPerStage, ++j) {
+        const int s = j % kGatherStages;
+        if (j >= kGatherStages) {  // the stage's previous rows have landed
+          const long long t0 = clock64();
+          while (!mbar_try_wait(smem_u32(&bars[warp][s]), ((j / kGatherStages) - 1) & 1, 1000u))
+            if (clock64() - t0 > kWaitLimitCycles) {
+              ok = false;
+              atomicOr(err, kErrWaitTimeout);
+              break;
+            }
+        }
+        if (!ok) break;
+        const int nr = min(kGatherRowsPerStage, r1 - r);
+        mbar_arrive_expect_tx(&bars[warp][s], (uint32_t)(nr * row_bytes));
+        for (int q = 0; q < nr; ++q)
+          bulk_g2s(ring + (uint32_t)((s * kGatherRowsPerStage + q) * row_bytes),
+                   kv + (int64_t)__ldg(rows + r + q) * row_stride, (uint32_t)row_bytes, &bars[warp][s]);
+      }
+      // drain: every stage still in flight lands before the CTA exits (the
+      // last chunk c that used stage s is waited for)
+      for (int s = 0; s < kGatherStages && s < j; ++s) {
+        const int c = s + kGatherStages * ((j - 1 - s) / kGatherStages);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_u32(&bars[warp][s]), (c / kGatherStages) & 1, 1000u))
+          if (clock64() - t0 > kWaitLimitCycles) {
+            atomicOr(err, kErrWaitTimeout);
+            break;
+          }
+      }
+      x = *reinterpret_cast<const uint32_t*>(gsm + (size_t)warp * kGatherStages * kGatherRowsPerStage * row_bytes);
+    }
+  }
+  sink[blockIdx.x * kGatherThreads + threadIdx.x] = x;
+}
+
+}  // namespace
+
+cudaError_t launch_gather_rate(int mechanism, const void* kv, int64_t row_stride, int row_bytes,
+                               const int32_t* rows, int n, uint32_t* sink, int* err, cudaStream_t stream) {
+  const int ctas = 148;
+  const size_t smem = mechanism == 1 ? (size_t)8 * kGatherStages * kGatherRowsPerStage * row_bytes : 0;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
+    e = cudaFuncSetAttribute(gather_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done[dev] = true;
+  }
+  gather_rate_kernel<<<ctas, kGatherThreads, smem, stream>>>(mechanism, static_cast<const uint8_t*>(kv),
+                                                            row_stride, row_bytes, rows, n, sink, err);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv4b

@@ -37,7 +37,7 @@ EXPORTED = (
     "dsv4b_kv_cache_write_status", "dsv4b_kv_write_selftest",
     "dsv4b_mqa_logits_metadata", "dsv4b_fp8_paged_mqa_logits", "dsv4b_mqa_logits_status",
     "dsv4b_set_test_stall", "dsv4b_prefill_workspace_bytes", "dsv4b_sparse_prefill",
-    "dsv4b_mma_rate_probe",
+    "dsv4b_mma_rate_probe", "dsv4b_gather_rate_probe",
 )
 
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -110,6 +110,9 @@ def _load():
     lib.dsv4b_sparse_decode_noalloc.argtypes = [P, _vp, _vp, ctypes.c_int, _vp]
     lib.dsv4b_read_kernel_status.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int), _vp]
     lib.dsv4b_set_test_stall.argtypes = [ctypes.c_int]
+    lib.dsv4b_gather_rate_probe.restype = ctypes.c_int
+    lib.dsv4b_gather_rate_probe.argtypes = [ctypes.c_int, _vp, _i64, ctypes.c_int, _vp, ctypes.c_int, _vp,
+                                            ctypes.c_size_t, _vp]
     lib.dsv4b_mma_rate_probe.restype = ctypes.c_int
     lib.dsv4b_mma_rate_probe.argtypes = [ctypes.c_int, ctypes.c_int, _vp, _vp]
     lib.dsv4b_prefill_workspace_bytes.restype = ctypes.c_size_t

@@ -199,6 +199,19 @@ DSV4B_API int dsv4b_gather_dequant(int layout, const void* kv, int num_blocks,
  * backs the tensor-core figures of the decode roofline. */
 DSV4B_API int dsv4b_mma_rate_probe(int shape, int ctas, long long* out, void* stream);
 
+/* Measurement: gather the n rows listed in `rows` (row_bytes each, a
+ * multiple of 16 up to 1536, at kv + row * row_stride) into 148 CTAs with
+ * one mechanism and nothing else running: 0 = 16-byte register loads by
+ * 256 threads per CTA, 1 = one cp.async.bulk per row into a shared-memory
+ * ring (8 issuing lanes per CTA).  scratch (device, >= (148 * 256 + 4) * 4
+ * bytes): a sink for the loaded words, then an int status word (set to a
+ * nonzero value if a bounded wait gave up; the caller zeroes it).  Time it
+ * with events on `stream`.  No reference counterpart: it backs the
+ * gather-ceiling figures of the decode roofline. */
+DSV4B_API int dsv4b_gather_rate_probe(int mechanism, const void* kv, int64_t row_stride, int row_bytes,
+                                      const int32_t* rows, int n, void* scratch, size_t scratch_bytes,
+                                      void* stream);
+
 /* KV-cache writer: quantise n bf16 tokens into the cache's FP8 format and
  * scatter them to their slots (flat page * page_block_size + offset).
  *   layout V32:    nope = latent [n, 512], rope = [n, 64]; 656-B records

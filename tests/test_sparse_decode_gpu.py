@@ -456,3 +456,27 @@ def test_mma_rate_probe_reports_every_shape():
         assert (v[:, 1] == mmas).all(), v
         assert (v[:, 0] > 0).all(), v
     assert _lib.lib.dsv4b_mma_rate_probe(6, 4, out.data_ptr(), None) == -1
+
+
+@pytest.mark.gpu
+def test_gather_rate_probe_runs_both_mechanisms():
+    """dsv4b_gather_rate_probe (the measurement behind the gather ceiling)
+    gathers rows with both mechanisms, its bounded waits all complete, and
+    it refuses bad arguments."""
+    import torch
+    from deepseek_v4_kernel import _lib
+    torch.cuda.set_device(0)
+    kv = torch.randint(0, 255, (4096 * 656,), dtype=torch.uint8, device="cuda")
+    rows = torch.randint(0, 4096, (3000,), dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(148 * 256 + 4, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for mech in (0, 1):
+        rc = _lib.lib.dsv4b_gather_rate_probe(mech, kv.data_ptr(), 656, 656, rows.data_ptr(), 3000,
+                                              scratch.data_ptr(), scratch.numel() * 4, s)
+        assert rc == 0, _lib.STATUS.get(rc, rc)
+    torch.cuda.synchronize()
+    assert int(scratch[-4].item()) == 0
+    assert _lib.lib.dsv4b_gather_rate_probe(2, kv.data_ptr(), 656, 656, rows.data_ptr(), 3000,
+                                            scratch.data_ptr(), scratch.numel() * 4, s) == -1
+    assert _lib.lib.dsv4b_gather_rate_probe(0, kv.data_ptr(), 656, 650, rows.data_ptr(), 3000,
+                                            scratch.data_ptr(), scratch.numel() * 4, s) == -1
