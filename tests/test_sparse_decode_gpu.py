@@ -178,11 +178,12 @@ def test_split_counts_agree(parts):
 
 @pytest.mark.parametrize("b,s_q,topk,parts", [(2, 1, 64, 148), (2, 1, 256, 74), (32, 1, 2048, 148),
                                               (3, 1, 1000, 7), (5, 3, 900, 148), (200, 1, 512, 148),
-                                              (1, 1, 4096, 148)])
+                                              (1, 1, 4096, 148), (20, 1, 512, 8), (33, 1, 256, 148)])
 def test_scheduler_records_match_oracle(b, s_q, topk, parts):
     """The device scheduler's records equal the restated plan, in both the
     row-aligned (rows <= parts) and the contiguous mode, including row
-    counts whose shared-memory tables start at odd offsets."""
+    counts whose shared-memory tables start at odd offsets, on both sides of
+    the single-warp scheduler's 32-row limit."""
     from deepseek_v4_kernel import ops
     spec = _kc().BatchSpec(b=b, s_q=s_q, h_q=64, topk=topk, ctx=8192, page_block=64, seed=3)
     bt = _kc().make_batch(spec)
