@@ -89,6 +89,8 @@ int check_prefill_params(const dsv4b_decode_params* p) {
   if (p->prefill != 1 || p->lse_includes_sink != 0 || p->extra_kv) return DSV4B_ERR_INVALID_ARGUMENT;
   if (p->b <= 0 || p->s_q != 1 || p->h_q <= 0 || p->topk <= 0) return DSV4B_ERR_INVALID_ARGUMENT;
   if (p->b > kMaxPrefillRows || p->h_q > 65535 * 64) return DSV4B_ERR_UNSUPPORTED;
+  // one grid column of tokens x 64-head groups
+  if ((int64_t)p->b * ((p->h_q + 63) / 64) > 2147483647) return DSV4B_ERR_UNSUPPORTED;
   if (p->d_v != 512) return DSV4B_ERR_UNSUPPORTED;
   if (p->d_qk != (p->layout == DSV4B_LAYOUT_BF16_576 ? 576 : 512)) return DSV4B_ERR_INVALID_ARGUMENT;
   if (!p->q || !p->indices || !p->out || !p->lse || !p->kv) return DSV4B_ERR_INVALID_ARGUMENT;
